@@ -1,0 +1,498 @@
+// Expert fetch (pinned host -> device cache slots) and the device slot allocator.
+//
+// Replaces the reference's csrc/fetch_experts.cu (fetch_kernel :49-69, host
+// wrapper :76-94, device_ptr_of :40-47) and bin/devcache.py's Triton
+// _resolve_slots (:45-98) / _fetch_experts (:101-130) / dev_resolve_and_fetch
+// (:230-255).
+//
+// Why a kernel and not a memcpy: a captured cudaMemcpyAsync bakes its source
+// address, so a replayed graph would keep copying the capture-time expert.
+// These kernels read the job table (which expert, which slot, how many) from
+// device memory when they run, so one captured graph serves whatever the
+// router picks on each replay.
+//
+// B200 design:
+//  * The allocator is one warp: the victim search (argmin of C stamps, lowest
+//    index on ties) is a warp-parallel scan over a shared-memory copy of the
+//    stamps plus a shuffle reduction, instead of the reference's serial O(k*C)
+//    single-thread loop.  Decisions stay sequential over the k ids, exactly as
+//    the reference orders them.
+//  * The fetch moves all buffers of all missed experts in ONE launch with a
+//    fixed grid (one CTA per SM by default): the jobs' bytes form one flat
+//    range that every CTA strides over, so even a single miss is spread over
+//    the whole grid and keeps enough 512-byte warp requests in flight to fill
+//    the host link.  Loads are 16-byte vector loads of mapped host memory that
+//    bypass L1; stores are plain (the GEMM reads the slot from L2 next).
+//  * The fetch launch depends on the allocator launch programmatically
+//    (griddepcontrol), so its CTAs are resident before the allocator ends.
+
+#include "d3_common.cuh"
+
+#include <stdlib.h>
+#include <string.h>
+
+namespace d3 {
+
+// ---------------------------------------------------------------- status
+
+static thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(D3_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) v = getenv("D3_NO_PDL") ? 0 : 1;
+  return v == 1;
+}
+
+// ---------------------------------------------------------------- kernels
+
+// Reference-compatible per-buffer fetch: grid (blocks_per_job, max_jobs).
+// Job j copies expert idx[j] into slot[j]; CTAs of jobs >= *njobs retire.
+__global__ void __launch_bounds__(256) fetch_jobs_kernel(const uint4* __restrict__ src,
+                                                         uint4* __restrict__ dst,
+                                                         const int32_t* __restrict__ idx,
+                                                         const int32_t* __restrict__ slot,
+                                                         const int32_t* __restrict__ njobs,
+                                                         int64_t vec_per_expert) {
+  const int j = blockIdx.y;
+  if (j >= *njobs) return;
+  const uint4* s = src + (int64_t)idx[j] * vec_per_expert;
+  uint4* d = dst + (int64_t)slot[j] * vec_per_expert;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // four independent 16-byte loads in flight per thread before any store
+  for (; i + 3 * stride < vec_per_expert; i += 4 * stride) {
+    uint4 a = ld_stream_u4(s + i), b = ld_stream_u4(s + i + stride);
+    uint4 c = ld_stream_u4(s + i + 2 * stride), e = ld_stream_u4(s + i + 3 * stride);
+    d[i] = a;
+    d[i + stride] = b;
+    d[i + 2 * stride] = c;
+    d[i + 3 * stride] = e;
+  }
+  for (; i < vec_per_expert; i += stride) d[i] = ld_stream_u4(s + i);
+}
+
+struct FetchParams {
+  const uint4* host[D3_MAX_BUFFERS];
+  uint4* cache[D3_MAX_BUFFERS];
+  int64_t vecs[D3_MAX_BUFFERS];   // 16-byte vectors per expert, per buffer
+  int64_t vec_total;              // sum over buffers
+  int32_t nbuf;
+  const int32_t* fetch_slot;
+  const int32_t* fetch_expert;
+  const int32_t* nmiss;
+};
+
+constexpr int kFetchThreads = 256;
+constexpr int kFetchUnroll = 4;
+
+// Flat multi-buffer fetch: the byte range of job j / buffer b / vector v is
+// linearised as j*vec_total + (prefix_b + v); CTAs stride over chunks of
+// kFetchThreads*kFetchUnroll vectors (16 KiB).
+__global__ void __launch_bounds__(kFetchThreads) fetch_layer_kernel(FetchParams p) {
+  pdl_wait();  // the allocator's job table must be complete
+  const int nm = *p.nmiss;
+  if (nm <= 0) return;
+  const int64_t total = (int64_t)nm * p.vec_total;
+  constexpr int64_t kChunk = (int64_t)kFetchThreads * kFetchUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * kChunk; base < total;
+       base += (int64_t)gridDim.x * kChunk) {
+    uint4 v[kFetchUnroll];
+    uint4* dptr[kFetchUnroll];
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u) {
+      const int64_t g = base + (int64_t)u * kFetchThreads + threadIdx.x;
+      dptr[u] = nullptr;
+      if (g < total) {
+        const int64_t j = g / p.vec_total;
+        int64_t r = g - j * p.vec_total;
+        int b = 0;
+        while (b < p.nbuf - 1 && r >= p.vecs[b]) { r -= p.vecs[b]; ++b; }
+        const int64_t e = p.fetch_expert[j], s = p.fetch_slot[j];
+        v[u] = ld_stream_u4(p.host[b] + e * p.vecs[b] + r);
+        dptr[u] = p.cache[b] + s * p.vecs[b] + r;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u)
+      if (dptr[u]) *dptr[u] = v[u];
+  }
+}
+
+struct ResolveParams {
+  const void* ids;
+  int32_t ids_bytes;
+  int32_t k;
+  int32_t num_experts;
+  int32_t capacity;
+  int32_t policy;
+  int32_t* slot_of;
+  int32_t* slot_expert;
+  int64_t* stamp;
+  int64_t* step;
+  int64_t* freq;
+  int64_t* ins;
+  int32_t* out_slot;
+  int32_t* fetch_slot;
+  int32_t* fetch_expert;
+  int32_t* nmiss;
+  int64_t* counters;
+  int64_t expert_bytes;
+};
+
+__device__ __forceinline__ int32_t load_id(const void* ids, int bytes, int i) {
+  if (bytes == 8) {
+    const int64_t v = static_cast<const int64_t*>(ids)[i];
+    return (v < INT32_MIN || v > INT32_MAX) ? -1 : (int32_t)v;
+  }
+  return static_cast<const int32_t*>(ids)[i];
+}
+
+// Lexicographic (key, index) minimum across the warp.
+__device__ __forceinline__ void warp_argmin(int64_t& key, int& idx) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const int64_t ok = __shfl_xor_sync(0xffffffffu, key, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+    if (ok < key || (ok == key && oi < idx)) { key = ok; idx = oi; }
+  }
+}
+
+// One warp.  LRU: the _resolve_slots decision sequence.  LFU: victim is the
+// lexicographic min of (used this step, uses since insert, insertion seq).
+// Dynamic shared memory: stamp[C] (+ freq[C], ins[C] for LFU), int64.
+__global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
+  extern __shared__ int64_t sh[];
+  int64_t* s_stamp = sh;
+  int64_t* s_freq = sh + p.capacity;
+  int64_t* s_ins = sh + 2 * p.capacity;
+  const int lane = threadIdx.x;
+  const int C = p.capacity;
+  const bool lfu = p.policy == D3_POLICY_LFU;
+  pdl_trigger();  // the dependent fetch grid may start launching now
+  for (int c = lane; c < C; c += 32) {
+    s_stamp[c] = p.stamp[c];
+    if (lfu) { s_freq[c] = p.freq[c]; s_ins[c] = p.ins[c]; }
+  }
+  const int64_t step = *p.step + 1;
+  __syncwarp();
+  int nmiss = 0, hits = 0;
+  for (int i = 0; i < p.k; ++i) {
+    const int32_t e = load_id(p.ids, p.ids_bytes, i);
+    if (e < 0 || e >= p.num_experts) {
+      if (lane == 0) p.out_slot[i] = -1;
+      continue;
+    }
+    int32_t s = lane == 0 ? p.slot_of[e] : 0;  // lane 0 owns all table reads/writes
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (s < 0) {
+      int64_t key;
+      int best = 0x7fffffff;
+      if (!lfu) {
+        key = INT64_MAX;
+        for (int c = lane; c < C; c += 32)
+          if (s_stamp[c] < key) { key = s_stamp[c]; best = c; }
+        warp_argmin(key, best);
+      } else {
+        // three-part key, reduced lexicographically
+        int64_t bu = INT64_MAX, bf = INT64_MAX, bi = INT64_MAX;
+        for (int c = lane; c < C; c += 32) {
+          const int64_t u = s_stamp[c] == step ? 1 : 0, f = s_freq[c], n = s_ins[c];
+          if (u < bu || (u == bu && (f < bf || (f == bf && (n < bi || (n == bi && c < best)))))) {
+            bu = u; bf = f; bi = n; best = c;
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          const int64_t ou = __shfl_xor_sync(0xffffffffu, bu, off);
+          const int64_t of = __shfl_xor_sync(0xffffffffu, bf, off);
+          const int64_t on = __shfl_xor_sync(0xffffffffu, bi, off);
+          const int oc = __shfl_xor_sync(0xffffffffu, best, off);
+          if (ou < bu || (ou == bu && (of < bf || (of == bf && (on < bi || (on == bi && oc < best)))))) {
+            bu = ou; bf = of; bi = on; best = oc;
+          }
+        }
+      }
+      if (lane == 0) {
+        const int32_t victim = p.slot_expert[best];
+        if (victim >= 0) p.slot_of[victim] = -1;
+        p.slot_of[e] = best;
+        p.slot_expert[best] = e;
+        p.fetch_slot[nmiss] = best;
+        p.fetch_expert[nmiss] = e;
+        if (lfu) {
+          s_freq[best] = 0;
+          s_ins[best] = (step << 8) | i;
+        }
+      }
+      ++nmiss;
+      s = best;
+    } else {
+      ++hits;
+    }
+    if (lane == 0) {
+      s_stamp[s] = step;
+      p.stamp[s] = step;
+      if (lfu) {
+        s_freq[s] += 1;
+        p.freq[s] = s_freq[s];
+        p.ins[s] = s_ins[s];
+      }
+      p.out_slot[i] = s;
+    }
+    __syncwarp();  // lane 0's shared-memory stamp update is seen by the next scan
+  }
+  if (lane == 0) {
+    *p.step = step;
+    *p.nmiss = nmiss;
+    if (p.counters) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 0), 1ull);
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 1), (unsigned long long)hits);
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 2), (unsigned long long)nmiss);
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 3),
+                (unsigned long long)(nmiss * p.expert_bytes));
+    }
+  }
+}
+
+__global__ void lookup_kernel(const int32_t* __restrict__ slot_of, int32_t E, const void* ids,
+                              int32_t ids_bytes, int32_t n, int32_t* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t e = load_id(ids, ids_bytes, i);
+  out[i] = (e >= 0 && e < E) ? slot_of[e] : -1;
+}
+
+// ---------------------------------------------------------------- host side
+
+static int launch_resolve(const ResolveParams& p, cudaStream_t st) {
+  const size_t smem = (size_t)p.capacity * sizeof(int64_t) * (p.policy == D3_POLICY_LFU ? 3 : 1);
+  if (smem > 48 * 1024) {
+    D3_CUDA_TRY(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "resolve smem attribute");
+  }
+  resolve_kernel<<<1, 32, smem, st>>>(p);
+  return launch_status("resolve_kernel launch");
+}
+
+static int make_fetch_params(const d3_layer_cache* L, FetchParams* fp, int64_t* expert_bytes) {
+  *expert_bytes = 0;
+  for (int b = 0; b < L->nbuf; ++b) {
+    D3_CHECK_ARG(L->host[b] && L->cache[b], "buffer %d: null host or cache pointer", b);
+    if (L->bytes[b] <= 0 || L->bytes[b] % 16)
+      return fail(D3_ERR_MISALIGNED, "buffer %d: bytes per expert %lld not a multiple of 16", b,
+                  (long long)L->bytes[b]);
+    if (!aligned16(L->host[b]) || !aligned16(L->cache[b]))
+      return fail(D3_ERR_MISALIGNED, "buffer %d: base pointer not 16 B aligned", b);
+    fp->host[b] = static_cast<const uint4*>(L->host[b]);
+    fp->cache[b] = static_cast<uint4*>(L->cache[b]);
+    fp->vecs[b] = L->bytes[b] / 16;
+    fp->vec_total += fp->vecs[b];
+    *expert_bytes += L->bytes[b];
+  }
+  fp->nbuf = L->nbuf;
+  fp->fetch_slot = L->fetch_slot;
+  fp->fetch_expert = L->fetch_expert;
+  fp->nmiss = L->nmiss;
+  return D3_OK;
+}
+
+// One fetch launch; with `pdl` it may start before the preceding allocator
+// launch finishes (its griddepcontrol.wait then blocks until that grid's
+// writes are visible).
+static int launch_fetch(const FetchParams& fp, int fetch_ctas, cudaStream_t st, bool pdl) {
+  const int ctas = fetch_ctas > 0 ? fetch_ctas : num_sms();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kFetchThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  D3_CUDA_TRY(cudaLaunchKernelEx(&cfg, fetch_layer_kernel, fp), "fetch_layer_kernel launch");
+  return D3_OK;
+}
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" {
+
+const char* d3_last_error(void) { return g_last_error; }
+
+int d3_abi_version(void) { return 1; }
+
+const char* d3_status_string(int status) {
+  switch (status) {
+    case D3_OK: return "D3_OK";
+    case D3_ERR_INVALID_ARG: return "D3_ERR_INVALID_ARG";
+    case D3_ERR_NOT_PINNED: return "D3_ERR_NOT_PINNED";
+    case D3_ERR_MISALIGNED: return "D3_ERR_MISALIGNED";
+    case D3_ERR_CUDA: return "D3_ERR_CUDA";
+    case D3_ERR_UNSUPPORTED: return "D3_ERR_UNSUPPORTED";
+    case D3_ERR_TOO_LARGE: return "D3_ERR_TOO_LARGE";
+    case D3_ERR_WORKSPACE: return "D3_ERR_WORKSPACE";
+    default: return "D3_ERR_UNKNOWN";
+  }
+}
+
+int d3_device_ptr_of(const void* host, size_t bytes, void** dev_out) {
+  D3_CHECK_ARG(host && dev_out, "d3_device_ptr_of: null pointer");
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, host);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(e, "cudaPointerGetAttributes");
+  }
+  if (attr.type != cudaMemoryTypeHost)
+    return fail(D3_ERR_NOT_PINNED,
+                "expected page-locked (pinned) host memory; pointer %p has memory type %d", host,
+                (int)attr.type);
+  void* dptr = nullptr;
+  D3_CUDA_TRY(cudaHostGetDevicePointer(&dptr, const_cast<void*>(host), 0),
+              "cudaHostGetDevicePointer");
+  // the whole range must lie in one mapped allocation
+  if (bytes > 1) {
+    cudaPointerAttributes last;
+    const char* end = static_cast<const char*>(host) + bytes - 1;
+    e = cudaPointerGetAttributes(&last, end);
+    if (e != cudaSuccess || last.type != cudaMemoryTypeHost) {
+      cudaGetLastError();
+      return fail(D3_ERR_NOT_PINNED, "range [%p, +%zu) leaves the pinned allocation", host, bytes);
+    }
+  }
+  *dev_out = dptr;
+  return D3_OK;
+}
+
+int d3_fetch_experts(const void* src_dev_base, void* dst, const int32_t* idx, const int32_t* slot,
+                     const int32_t* njobs, int64_t expert_bytes, int32_t max_jobs,
+                     int32_t blocks_per_job, int32_t threads, d3_stream_t stream) {
+  D3_CHECK_ARG(src_dev_base && dst && idx && slot && njobs, "d3_fetch_experts: null pointer");
+  if (expert_bytes <= 0 || expert_bytes % 16)
+    return fail(D3_ERR_MISALIGNED, "expert_bytes must be a positive multiple of 16 (got %lld)",
+                (long long)expert_bytes);
+  if (!aligned16(src_dev_base)) return fail(D3_ERR_MISALIGNED, "host base must be 16 B aligned");
+  if (!aligned16(dst)) return fail(D3_ERR_MISALIGNED, "cache base must be 16 B aligned");
+  D3_CHECK_ARG(threads == 256, "threads must be 256 (kernel built with __launch_bounds__(256))");
+  D3_CHECK_ARG(max_jobs >= 1 && max_jobs <= 65535, "max_jobs out of range");
+  D3_CHECK_ARG(blocks_per_job >= 1 && blocks_per_job <= 65535, "blocks_per_job out of range");
+  if (max_jobs == 0) return D3_OK;
+  const dim3 grid((unsigned)blocks_per_job, (unsigned)max_jobs);
+  fetch_jobs_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint4*>(src_dev_base), static_cast<uint4*>(dst), idx, slot, njobs,
+      expert_bytes / 16);
+  return launch_status("fetch_jobs_kernel launch");
+}
+
+int d3_resolve_slots(const void* ids, int32_t ids_bytes, int32_t k, int32_t* slot_of,
+                     int32_t num_experts, int32_t* slot_expert, int64_t* stamp, int32_t capacity,
+                     int32_t* out_slot, int32_t* fetch_slot, int32_t* fetch_expert, int32_t* nmiss,
+                     int64_t* step, d3_stream_t stream) {
+  D3_CHECK_ARG(ids && slot_of && slot_expert && stamp && out_slot && fetch_slot && fetch_expert &&
+                   nmiss && step,
+               "d3_resolve_slots: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
+  D3_CHECK_ARG(num_experts >= 1, "num_experts must be >= 1");
+  if (capacity < 1 || capacity > 8192)
+    return fail(D3_ERR_TOO_LARGE, "capacity must be in [1, 8192] (got %d)", capacity);
+  ResolveParams p{};
+  p.ids = ids; p.ids_bytes = ids_bytes; p.k = k; p.num_experts = num_experts;
+  p.capacity = capacity; p.policy = D3_POLICY_LRU;
+  p.slot_of = slot_of; p.slot_expert = slot_expert; p.stamp = stamp; p.step = step;
+  p.out_slot = out_slot; p.fetch_slot = fetch_slot; p.fetch_expert = fetch_expert;
+  p.nmiss = nmiss;
+  return launch_resolve(p, (cudaStream_t)stream);
+}
+
+int d3_resolve_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
+                     int32_t fetch_ctas, d3_stream_t stream) {
+  D3_CHECK_ARG(L && ids, "d3_resolve_fetch: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
+  D3_CHECK_ARG(L->num_experts >= 1, "num_experts must be >= 1");
+  if (L->capacity < 1 || L->capacity > 8192)
+    return fail(D3_ERR_TOO_LARGE, "capacity must be in [1, 8192] (got %d)", L->capacity);
+  D3_CHECK_ARG(L->policy == D3_POLICY_LRU || L->policy == D3_POLICY_LFU, "unknown policy %d",
+               L->policy);
+  D3_CHECK_ARG(L->nbuf >= 1 && L->nbuf <= D3_MAX_BUFFERS, "nbuf must be in [1, %d]",
+               D3_MAX_BUFFERS);
+  D3_CHECK_ARG(L->slot_of && L->slot_expert && L->stamp && L->step && L->out_slot &&
+                   L->fetch_slot && L->fetch_expert && L->nmiss,
+               "d3_resolve_fetch: null table pointer");
+  if (L->policy == D3_POLICY_LFU)
+    D3_CHECK_ARG(L->freq && L->ins, "LFU needs freq and ins tables");
+  D3_CHECK_ARG(fetch_ctas >= 0 && fetch_ctas <= 65535, "fetch_ctas out of range");
+  FetchParams fp{};
+  int64_t expert_bytes = 0;
+  int rc = make_fetch_params(L, &fp, &expert_bytes);
+  if (rc) return rc;
+
+  ResolveParams p{};
+  p.ids = ids; p.ids_bytes = ids_bytes; p.k = k; p.num_experts = L->num_experts;
+  p.capacity = L->capacity; p.policy = L->policy;
+  p.slot_of = L->slot_of; p.slot_expert = L->slot_expert; p.stamp = L->stamp; p.step = L->step;
+  p.freq = L->freq; p.ins = L->ins;
+  p.out_slot = L->out_slot; p.fetch_slot = L->fetch_slot; p.fetch_expert = L->fetch_expert;
+  p.nmiss = L->nmiss; p.counters = L->counters; p.expert_bytes = expert_bytes;
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = launch_resolve(p, st);
+  if (rc) return rc;
+  return launch_fetch(fp, fetch_ctas, st, pdl_enabled());
+}
+
+int d3_fetch_jobs(const d3_layer_cache* L, int32_t fetch_ctas, d3_stream_t stream) {
+  D3_CHECK_ARG(L, "d3_fetch_jobs: null descriptor");
+  D3_CHECK_ARG(L->nbuf >= 1 && L->nbuf <= D3_MAX_BUFFERS, "nbuf must be in [1, %d]",
+               D3_MAX_BUFFERS);
+  D3_CHECK_ARG(L->fetch_slot && L->fetch_expert && L->nmiss, "d3_fetch_jobs: null job table");
+  D3_CHECK_ARG(fetch_ctas >= 0 && fetch_ctas <= 65535, "fetch_ctas out of range");
+  FetchParams fp{};
+  int64_t expert_bytes = 0;
+  int rc = make_fetch_params(L, &fp, &expert_bytes);
+  if (rc) return rc;
+  return launch_fetch(fp, fetch_ctas, (cudaStream_t)stream, false);
+}
+
+int d3_lookup_slots(const int32_t* slot_of, int32_t num_experts, const void* ids,
+                    int32_t ids_bytes, int32_t n, int32_t* slot_out, d3_stream_t stream) {
+  D3_CHECK_ARG(slot_of && ids && slot_out, "d3_lookup_slots: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(n >= 0, "n must be >= 0");
+  if (n == 0) return D3_OK;
+  lookup_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(slot_of, num_experts, ids,
+                                                                    ids_bytes, n, slot_out);
+  return launch_status("lookup_kernel launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+/*
+ * d3b200 -- B200 (sm_100a) routed-MoE expert offload hot path, C ABI.
+ *
+ * One shared library (libd3b200.so) with plain C entry points: raw pointers,
+ * sizes and a CUDA stream, an int status return (D3_OK == 0, negative on
+ * error), no exceptions across the ABI and no device or host allocation inside
+ * any call.  Every launch goes on the caller's stream, issues no host sync and
+ * keeps a static launch shape, so every call below (except d3_device_ptr_of,
+ * which queries the driver) can be recorded into a CUDA graph and replayed;
+ * device-side tables are read at replay time, never baked at capture.
+ *
+ * Device pointers: int32/int64 tables and byte buffers allocated by the caller
+ * (e.g. torch tensors).  Host expert storage must be page-locked and mapped
+ * (cudaHostAlloc / torch pin_memory); pass the pointer d3_device_ptr_of gives.
+ *
+ * Each entry point names the reference interface it replaces
+ * (darth-feir/drama3-offloading, path:line).
+ */
+#ifndef D3B200_H
+#define D3B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define D3_API __attribute__((visibility("default")))
+#else
+#define D3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t, passed as an opaque pointer (0 = legacy default stream). */
+typedef void* d3_stream_t;
+
+enum {
+  D3_OK = 0,
+  D3_ERR_INVALID_ARG = -1,   /* bad size, null pointer, out-of-range parameter */
+  D3_ERR_NOT_PINNED = -2,    /* host pointer is not page-locked / not mapped */
+  D3_ERR_MISALIGNED = -3,    /* pointer or byte count not 16-byte aligned */
+  D3_ERR_CUDA = -4,          /* a CUDA runtime/driver call failed (see d3_last_error) */
+  D3_ERR_UNSUPPORTED = -5,   /* shape or device not supported by this build */
+  D3_ERR_TOO_LARGE = -6,     /* exceeds a documented maximum */
+  D3_ERR_WORKSPACE = -7      /* workspace pointer null or smaller than required */
+};
+
+/* Human-readable name of a status code (static string). */
+D3_API const char* d3_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+D3_API const char* d3_last_error(void);
+/* ABI version: bumped on any incompatible change of these declarations. */
+D3_API int d3_abi_version(void);
+
+/* ------------------------------------------------------------------ fetch */
+
+/* Device-visible address of page-locked host memory [host, host+bytes).
+ * Fails with D3_ERR_NOT_PINNED for pageable memory.
+ * Replaces device_ptr_of(at::Tensor) -- csrc/fetch_experts.cu:40-47. */
+D3_API int d3_device_ptr_of(const void* host, size_t bytes, void** dev_out);
+
+/* Copy expert idx[j] (expert_bytes each, from src_dev_base) into cache slot
+ * slot[j] of dst for every j < *njobs (njobs is read on the device at run
+ * time; launched as max_jobs x blocks_per_job CTAs of `threads` threads, the
+ * surplus retiring without writing).  Requires 16-byte aligned src, dst and
+ * expert_bytes, threads == 256.
+ * Replaces fetch_experts(...) -- csrc/fetch_experts.cu:76-94; the semantics
+ * of _fetch_experts -- bin/devcache.py:101-130. */
+D3_API int d3_fetch_experts(const void* src_dev_base, void* dst, const int32_t* idx,
+                     const int32_t* slot, const int32_t* njobs, int64_t expert_bytes,
+                     int32_t max_jobs, int32_t blocks_per_job, int32_t threads,
+                     d3_stream_t stream);
+
+/* --------------------------------------------------------------- allocator */
+
+/* One LRU resolve of k expert ids into cache slots, exactly the semantics of
+ * _resolve_slots -- bin/devcache.py:45-98: step is bumped on the device; for
+ * each id in order a hit keeps its slot, a miss takes the slot with the
+ * smallest stamp (lowest index on ties), clears the victim's slot_of entry and
+ * queues (fetch_slot, fetch_expert); every used slot is stamped with the new
+ * step; *nmiss receives the number of queued fetches.  ids are int32
+ * (ids_bytes == 4) or int64 (ids_bytes == 8, e.g. torch.topk output).
+ * Ids outside [0, num_experts) get out_slot = -1 and are not fetched.
+ * Limits: 1 <= k <= 64, 1 <= capacity <= 8192. */
+D3_API int d3_resolve_slots(const void* ids, int32_t ids_bytes, int32_t k, int32_t* slot_of,
+                     int32_t num_experts, int32_t* slot_expert, int64_t* stamp,
+                     int32_t capacity, int32_t* out_slot, int32_t* fetch_slot,
+                     int32_t* fetch_expert, int32_t* nmiss, int64_t* step,
+                     d3_stream_t stream);
+
+enum { D3_POLICY_LRU = 0, D3_POLICY_LFU = 1 };
+enum { D3_MAX_BUFFERS = 4 };
+
+/* One layer's device expert cache: the tables init_dev_cache allocates
+ * (bin/devcache.py:146-167) plus the per-buffer host/cache byte layout
+ * _copy_pairs describes (bin/devcache.py:170-181).  Plain data, filled by the
+ * caller; the library never stores it. */
+typedef struct d3_layer_cache {
+  int32_t num_experts;      /* E */
+  int32_t capacity;         /* C slots */
+  int32_t policy;           /* D3_POLICY_LRU or D3_POLICY_LFU */
+  int32_t nbuf;             /* buffers per expert, 1..D3_MAX_BUFFERS */
+  int32_t* slot_of;         /* [E]  expert -> slot or -1 */
+  int32_t* slot_expert;     /* [C]  slot -> expert or -1 */
+  int64_t* stamp;           /* [C]  step of last use */
+  int64_t* step;            /* [1]  call counter, bumped on device */
+  int64_t* freq;            /* [C]  LFU: uses since insertion (NULL for LRU) */
+  int64_t* ins;             /* [C]  LFU: insertion sequence (NULL for LRU) */
+  int32_t* out_slot;        /* [k]  resolved slot per id */
+  int32_t* fetch_slot;      /* [k]  queued fetch: destination slot */
+  int32_t* fetch_expert;    /* [k]  queued fetch: expert id */
+  int32_t* nmiss;           /* [1]  queued fetch count */
+  int64_t* counters;        /* [4]  cumulative {calls, hits, misses, bytes fetched}, or NULL */
+  const void* host[D3_MAX_BUFFERS];  /* device-visible pinned host base, [E][bytes[b]] */
+  void* cache[D3_MAX_BUFFERS];       /* device cache buffer, [C][bytes[b]] */
+  int64_t bytes[D3_MAX_BUFFERS];     /* bytes per expert of buffer b (multiple of 16) */
+} d3_layer_cache;
+
+/* Resolve k ids through layer->policy and fetch every miss's nbuf buffers from
+ * pinned host memory into its slot: one allocator launch and one fetch launch
+ * (a fixed grid of fetch_ctas CTAs; 0 = one per SM), dependent via
+ * programmatic launch.  Results: layer->out_slot[0..k).
+ * Replaces dev_resolve_and_fetch -- bin/devcache.py:230-255 (which issues
+ * _resolve_slots plus four fetch launches). */
+D3_API int d3_resolve_fetch(const d3_layer_cache* layer, const void* ids, int32_t ids_bytes,
+                     int32_t k, int32_t fetch_ctas, d3_stream_t stream);
+
+/* Only the fetch half of d3_resolve_fetch: copy the jobs already queued in
+ * layer->fetch_slot / fetch_expert / *nmiss (e.g. by d3_resolve_slots or a
+ * host-written job list) for all nbuf buffers, one launch of fetch_ctas CTAs
+ * (0 = one per SM).  The device job count may be 0..C; no allocator runs.
+ * Replaces the four per-buffer fetch launches of dev_resolve_and_fetch --
+ * bin/devcache.py:240-254. */
+D3_API int d3_fetch_jobs(const d3_layer_cache* layer, int32_t fetch_ctas, d3_stream_t stream);
+
+/* Read-only lookup (no stamp, no insert): slot_out[i] = slot_of[ids[i]] or -1.
+ * The prefill path's borrow from the device cache -- bin/offload.py:195-214. */
+D3_API int d3_lookup_slots(const int32_t* slot_of, int32_t num_experts, const void* ids,
+                    int32_t ids_bytes, int32_t n, int32_t* slot_out, d3_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* D3B200_H */
