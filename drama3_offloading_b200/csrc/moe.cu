@@ -1,0 +1,701 @@
+// Routed-MoE expert computation with block-scaled FP8 weights on sm_100a.
+//
+// Computes what the reference hands to upstream fp8_moe_forward(x, ids, w,
+// w13, s13, w2, s2) (call sites bin/devcache.py:275-277, bin/offload.py:177,
+// :239, :340, :388, :449): for every routed (token t, slot k) pair with expert
+// e = ids[t,k],
+//     h   = silu(x_t W_gate[e]^T) * (x_t W_up[e]^T)         (W13 rows [0,I) / [I,2I))
+//     out_t += w[t,k] * (h W_down[e]^T)
+// where W = e4m3 bytes x fp32 scale per 128x128 block.
+//
+// Pipeline (all launches static-shaped, sync-free, graph-capturable):
+//   1. route   one CTA: counting sort of the pairs by expert (stable), tile
+//              lists for both GEMMs (expert, 128-row M tile, N tile of pairs,
+//              K-split), written to the workspace.
+//   2. quant   activations of every sorted pair -> two e4m3 planes hi/lo per
+//              128-wide K block with one fp32 scale: x ~= s*(hi + lo), where
+//              hi = e4m3(x/s) and lo = e4m3(x/s - hi).  Two fp8 planes carry
+//              ~8 significant bits, i.e. bf16-class activations on the fp8
+//              tensor path.
+//   3. gemm1   tcgen05 kind::f8f6f4: D[128 weight rows, BN pairs] per K block
+//              = W.hi + W.lo accumulated in TMEM, TMA-staged operands (128B
+//              swizzle); the epilogue warps promote each K block with
+//              s_w[kb] * s_x[n,kb] into fp32 registers (per-block scales, the
+//              DeepSeek-style promotion), then store the K-split partials.
+//   4. act     sum the K-split partials, SwiGLU, quantise h into hi/lo planes.
+//   5. gemm2   same kernel over W2 (K = I).
+//   6. combine out[t] = bf16(sum_k w[t,k] * y[pair(t,k)]) in a fixed order.
+// Swap-AB: weight rows are the MMA M dimension (128), routed tokens the N
+// dimension (16 for decode-sized batches, 64 otherwise), so one decode token
+// still runs full-height MMAs.  The GEMMs stream each weight byte from HBM
+// once per N tile; K-splits spread a small batch's few experts over all SMs.
+#include "d3_common.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <mutex>
+
+namespace d3 {
+
+// ---------------------------------------------------------------- tensor maps
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D byte matrix [rows, cols] (row pitch = pitch bytes), box [box_rows, 128 B],
+// 128-byte swizzle.  Rows past `rows` read as zero.
+static int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
+                        uint64_t pitch, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(D3_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if (!aligned16(base) || pitch % 16)
+    return fail(D3_ERR_MISALIGNED, "tensor map base/pitch not 16-byte aligned");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(D3_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return D3_OK;
+}
+
+// ---------------------------------------------------------------- layout
+
+constexpr int kMaxExperts = 8192;
+constexpr int kMaxPairs = 65536;
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s per wait, then abort
+
+struct Plan {
+  int P;        // routed pairs = T * topk
+  int Ppad;     // P rounded up to a whole N tile (rows of the operand planes)
+  int n;        // experts in the weight arrays
+  int H, I;
+  int BN;       // pairs per N tile
+  int split1, kbps1;   // gemm1 K split count / K blocks per split (K = H)
+  int split2, kbps2;   // gemm2 (K = I)
+  int maxt1, maxt2;    // tile list capacities
+  // workspace offsets (bytes)
+  size_t o_cnt, o_off, o_sorted, o_inv, o_tiles1, o_tiles2, o_ntiles, o_xq, o_xs, o_ws1, o_hq,
+      o_hs, o_ws2, total;
+};
+
+static size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static void make_plan(Plan& p, int T, int topk, int n, int H, int I, int sms) {
+  p.P = T * topk; p.n = n; p.H = H; p.I = I;
+  const int distinct = p.P < n ? p.P : n;     // upper bound on experts hit
+  const double per_expert = (double)p.P / distinct;
+  p.BN = per_expert > 24.0 ? 64 : 16;
+  p.Ppad = (p.P + p.BN - 1) / p.BN * p.BN;
+  const int nt_bound = p.P / p.BN + distinct;  // sum_e ceil(c_e / BN)
+  // spread K so that the (experts x M tiles) of a small batch fill the SMs
+  auto split_for = [&](int mtiles, int nkb, int& split, int& kbps) {
+    const long base = (long)(p.P / p.BN + distinct) * mtiles;  // ~tiles without split
+    int want = (int)((2L * sms + base - 1) / (base > 0 ? base : 1));
+    if (want < 1) want = 1;
+    if (want > nkb) want = nkb;
+    kbps = (nkb + want - 1) / want;
+    split = (nkb + kbps - 1) / kbps;
+  };
+  split_for(2 * I / 128, H / 128, p.split1, p.kbps1);
+  split_for(H / 128, I / 128, p.split2, p.kbps2);
+  p.maxt1 = nt_bound * (2 * I / 128) * p.split1;
+  p.maxt2 = nt_bound * (H / 128) * p.split2;
+  size_t o = 0;
+  p.o_cnt = o;     o += al(sizeof(int) * (size_t)n);
+  p.o_off = o;     o += al(sizeof(int) * (size_t)n);
+  p.o_sorted = o;  o += al(sizeof(int) * (size_t)p.P);
+  p.o_inv = o;     o += al(sizeof(int) * (size_t)p.P);
+  p.o_tiles1 = o;  o += al(sizeof(int4) * (size_t)p.maxt1);
+  p.o_tiles2 = o;  o += al(sizeof(int4) * (size_t)p.maxt2);
+  p.o_ntiles = o;  o += al(sizeof(int) * 4);
+  p.o_xq = o;      o += al((size_t)p.Ppad * 2 * H);
+  p.o_xs = o;      o += al(sizeof(float) * (size_t)p.Ppad * (H / 128));
+  p.o_ws1 = o;     o += al(sizeof(float) * (size_t)p.split1 * p.P * 2 * I);
+  p.o_hq = o;      o += al((size_t)p.Ppad * 2 * I);
+  p.o_hs = o;      o += al(sizeof(float) * (size_t)p.Ppad * (I / 128));
+  p.o_ws2 = o;     o += al(sizeof(float) * (size_t)p.split2 * p.P * H);
+  p.total = o;
+}
+
+// ---------------------------------------------------------------- 1. route
+
+struct RouteParams {
+  const void* ids; int ids_bytes; int P; int n;
+  int* cnt; int* off; int* sorted; int* inv;
+  int4* tiles1; int4* tiles2; int* ntiles;
+  int BN;
+  int mt1, nkb1, kbps1, split1;
+  int mt2, nkb2, kbps2, split2;
+};
+
+__device__ __forceinline__ int load_pair_id(const void* ids, int bytes, int i, int n) {
+  long long v = bytes == 8 ? static_cast<const long long*>(ids)[i]
+                           : (long long)static_cast<const int*>(ids)[i];
+  return (v >= 0 && v < n) ? (int)v : -1;
+}
+
+__device__ __forceinline__ int4 pack_tile(int e, int m, int row0, int ncount, int kb0, int kb1) {
+  return make_int4(e, m, row0, ncount | (kb0 << 8) | (kb1 << 20));
+}
+
+// One CTA of 1024 threads; dynamic smem: cursor[n] + tile prefix[n].
+__global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
+  extern __shared__ int sm[];
+  int* cursor = sm;            // [n]
+  int* tcount = sm + p.n;      // [n] N tiles per expert, then its prefix
+  __shared__ int warp_tot[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < p.n; e += blockDim.x) cursor[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.P; i += blockDim.x) {
+    const int e = load_pair_id(p.ids, p.ids_bytes, i, p.n);
+    if (e >= 0) atomicAdd(&cursor[e], 1);
+    p.inv[i] = -1;
+  }
+  __syncthreads();
+  // exclusive scans of counts (-> offsets) and of N tiles per expert
+  const int per = (p.n + blockDim.x - 1) / blockDim.x;
+  const int lo = tid * per, hi = min(p.n, lo + per);
+  int s_cnt = 0, s_til = 0;
+  for (int e = lo; e < hi; ++e) {
+    const int c = cursor[e];
+    s_cnt += c;
+    s_til += (c + p.BN - 1) / p.BN;
+  }
+  // block scan of (s_cnt, s_til) packed as two ints via two passes
+  int v = s_cnt, w = s_til;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, v, o), b = __shfl_up_sync(0xffffffffu, w, o);
+    if (lane >= o) { v += a; w += b; }
+  }
+  __shared__ int wt2[32];
+  if (lane == 31) { warp_tot[warp] = v; wt2[warp] = w; }
+  __syncthreads();
+  if (warp == 0) {
+    int a = warp_tot[lane], b = wt2[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) { a += x; b += y; }
+    }
+    warp_tot[lane] = a; wt2[lane] = b;
+  }
+  __syncthreads();
+  int base_c = (v - s_cnt) + (warp > 0 ? warp_tot[warp - 1] : 0);
+  int base_t = (w - s_til) + (warp > 0 ? wt2[warp - 1] : 0);
+  const int total_ntiles = wt2[31];
+  for (int e = lo; e < hi; ++e) {
+    const int c = cursor[e];
+    p.cnt[e] = c;
+    p.off[e] = base_c;
+    const int t = (c + p.BN - 1) / p.BN;
+    tcount[e] = base_t;
+    cursor[e] = base_c;
+    base_c += c;
+    base_t += t;
+  }
+  __syncthreads();
+  // stable placement: warp 0 walks the pairs in order, 32 at a time
+  if (warp == 0) {
+    for (int b0 = 0; b0 < p.P; b0 += 32) {
+      const int i = b0 + lane;
+      const int e = i < p.P ? load_pair_id(p.ids, p.ids_bytes, i, p.n) : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      const int leader = __ffs(m) - 1;
+      const int rank = __popc(m & ((1u << lane) - 1));
+      int base = 0;
+      if (lane == leader && e >= 0) {
+        base = cursor[e];
+        cursor[e] = base + __popc(m);
+      }
+      base = __shfl_sync(0xffffffffu, base, leader);
+      if (e >= 0) {
+        const int pos = base + rank;
+        p.sorted[pos] = i;
+        p.inv[i] = pos;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // tile lists: for expert e, N tile j, split s, M tile m
+  const int per_nt1 = p.mt1 * p.split1, per_nt2 = p.mt2 * p.split2;
+  for (int e = lo; e < hi; ++e) {
+    const int c = p.cnt[e];
+    if (c == 0) continue;
+    const int ntl = (c + p.BN - 1) / p.BN;
+    const int t0 = tcount[e];
+    for (int j = 0; j < ntl; ++j) {
+      const int row0 = p.off[e] + j * p.BN;
+      const int nc = min(p.BN, c - j * p.BN);
+      int4* d1 = p.tiles1 + (size_t)(t0 + j) * per_nt1;
+      for (int s = 0; s < p.split1; ++s)
+        for (int m = 0; m < p.mt1; ++m)
+          d1[s * p.mt1 + m] = pack_tile(e, m, row0, nc, s * p.kbps1,
+                                        min(p.nkb1, (s + 1) * p.kbps1));
+      int4* d2 = p.tiles2 + (size_t)(t0 + j) * per_nt2;
+      for (int s = 0; s < p.split2; ++s)
+        for (int m = 0; m < p.mt2; ++m)
+          d2[s * p.mt2 + m] = pack_tile(e, m, row0, nc, s * p.kbps2,
+                                        min(p.nkb2, (s + 1) * p.kbps2));
+    }
+  }
+  if (tid == 0) {
+    p.ntiles[0] = total_ntiles * per_nt1;
+    p.ntiles[1] = total_ntiles * per_nt2;
+    p.ntiles[2] = warp_tot[31];  // valid (in-range) pairs
+  }
+}
+
+// ---------------------------------------------------------------- 2/4. quantise
+
+// hi/lo e4m3 planes of one 128-element block held 4 per lane: returns scale.
+__device__ __forceinline__ float quant_block(const float (&v)[4], uint32_t& hi4, uint32_t& lo4) {
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.f / amax : 0.f;
+  hi4 = 0; lo4 = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float y = v[q] * inv;
+    const __nv_fp8_storage_t h = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+    const float hf = __half2float(__nv_cvt_fp8_to_halfraw(h, __NV_E4M3));
+    const __nv_fp8_storage_t l = __nv_cvt_float_to_fp8(y - hf, __NV_SATFINITE, __NV_E4M3);
+    hi4 |= (uint32_t)h << (8 * q);
+    lo4 |= (uint32_t)l << (8 * q);
+  }
+  return amax > 0.f ? amax / 448.f : 0.f;
+}
+
+// One warp per (sorted row, K block): x row of the pair's token -> planes.
+// Rows past the valid pairs (and up to Ppad) become zeros.
+__global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted,
+                               int P, int Ppad, int topk, int H, uint8_t* __restrict__ xq,
+                               float* __restrict__ xs) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int nkb = H / 128;
+  if (gw >= Ppad * nkb) return;
+  const int row = gw / nkb, kb = gw - row * nkb;
+  const int pair = row < P ? sorted[row] : -1;
+  float v[4];
+  uint8_t* qrow = xq + (size_t)row * 2 * H;
+  if (pair < 0) {  // rows past the valid pairs (skipped ids)
+    v[0] = v[1] = v[2] = v[3] = 0.f;
+  } else {
+    const int t = pair / topk;
+    const __nv_bfloat16* src = x + (size_t)t * H + kb * 128 + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = __bfloat162float(b[q]);
+  }
+  uint32_t hi4, lo4;
+  const float s = quant_block(v, hi4, lo4);
+  *reinterpret_cast<uint32_t*>(qrow + kb * 128 + lane * 4) = hi4;
+  *reinterpret_cast<uint32_t*>(qrow + H + kb * 128 + lane * 4) = lo4;
+  if (lane == 0) xs[(size_t)row * nkb + kb] = s;
+}
+
+// One warp per (sorted row, K block of I): sum splits, SwiGLU, quantise.
+// Rows at or past the valid pair count (device word) become zeros.
+__global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int Ppad,
+                           const int* __restrict__ nvalid_ptr, int I, uint8_t* __restrict__ hq,
+                           float* __restrict__ hs) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int nkb = I / 128;
+  if (gw >= Ppad * nkb) return;
+  const int row = gw / nkb, kb = gw - row * nkb;
+  const int nsplit = row < *nvalid_ptr ? split : 0;
+  float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < nsplit; ++s) {
+    const float* r = ws1 + ((size_t)s * P + row) * 2 * I + kb * 128 + lane * 4;
+    const float4 a = *reinterpret_cast<const float4*>(r);
+    const float4 b = *reinterpret_cast<const float4*>(r + I);
+    g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
+    u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+  }
+  float h[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h[q] = g[q] / (1.f + expf(-g[q])) * u[q];
+  uint32_t hi4, lo4;
+  const float s = quant_block(h, hi4, lo4);
+  uint8_t* qrow = hq + (size_t)row * 2 * I;
+  *reinterpret_cast<uint32_t*>(qrow + kb * 128 + lane * 4) = hi4;
+  *reinterpret_cast<uint32_t*>(qrow + I + kb * 128 + lane * 4) = lo4;
+  if (lane == 0) hs[(size_t)row * nkb + kb] = s;
+}
+
+// out[t, j] = bf16( sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
+__global__ void combine_kernel(const float* __restrict__ ws2, int split, int P, int H,
+                               const int* __restrict__ inv, const void* __restrict__ weights,
+                               int weights_f32, int T, int topk, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= T || j >= H) return;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < topk; ++k) {
+    const int pos = inv[t * topk + k];
+    if (pos < 0) continue;
+    const float wk = weights_f32 ? static_cast<const float*>(weights)[t * topk + k]
+                                 : __bfloat162float(
+                                       static_cast<const __nv_bfloat16*>(weights)[t * topk + k]);
+    float y[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < split; ++s) {
+      const float4 a = *reinterpret_cast<const float4*>(ws2 + ((size_t)s * P + pos) * H + j);
+      y[0] += a.x; y[1] += a.y; y[2] += a.z; y[3] += a.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[q] = fmaf(wk, y[q], acc[q]);
+  }
+  __nv_bfloat16 o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) o[q] = __float2bfloat16_rn(acc[q]);
+  *reinterpret_cast<uint2*>(out + (size_t)t * H + j) = *reinterpret_cast<uint2*>(o);
+}
+
+// ---------------------------------------------------------------- 3/5. GEMM
+
+struct GemmParams {
+  const int4* tiles;
+  const int* ntiles;          // device count of valid tiles
+  const float* wscale;        // [n][mblocks][kblocks]
+  int rows_per_expert;        // weight rows per expert (2I or H)
+  int mblocks, kblocks;       // per expert, 128-granular
+  const float* xscale;        // [P][kblocks]
+  int K;                      // bytes per weight row = K elements
+  float* out;                 // [split][P][Mtot]
+  int P, Mtot, kbps;
+  int* err;                   // device error word (first failure wins)
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = BN <= 16 ? 8 : 6;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;  // power of two for 16/64
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  // warp 0 TMA, warp 1 MMA, then EPI epilogue warps; each epilogue thread owns
+  // one accumulator row (TMEM lane) and CPT of the BN columns
+  static constexpr int EPI = BN >= 64 ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI;
+  static constexpr int CPT = BN * 4 / EPI;
+};
+
+__device__ __forceinline__ void gemm_error(int* err, int code) { atomicCAS(err, 0, code); }
+
+template <int BN>
+__global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_x, GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;             // [S]
+  uint64_t* empty = bars + S;        // [S]
+  uint64_t* accf = bars + 2 * S;     // [2]
+  uint64_t* acce = bars + 2 * S + 2; // [2]
+  uint64_t* done = bars + 2 * S + 4; // [1]
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(accf + i, 1); mbar_init(acce + i, 32 * Cfg::EPI); }
+    mbar_init(done, 1);
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int ntiles = *p.ntiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+        const int4 tl = p.tiles[t];
+        const int e = tl.x, m = tl.y, row0 = tl.z;
+        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+        const int wrow = e * p.rows_per_expert + m * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1, kWaitBudgetNs)) {
+            gemm_error(p.err, 1); s_abort = 1; break;
+          }
+          uint8_t* a = stage_base + (size_t)stage * Cfg::STAGE_BYTES;
+          uint8_t* bh = a + Cfg::A_BYTES;
+          uint8_t* bl = bh + Cfg::B_BYTES;
+          mbar_arrive_expect_tx(full + stage, Cfg::STAGE_BYTES);
+          tma_load_2d(a, &tm_w, full + stage, kb * 128, wrow);
+          tma_load_2d(bh, &tm_x, full + stage, kb * 128, row0);
+          tma_load_2d(bl, &tm_x, full + stage, p.K + kb * 128, row0);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t it = 0;  // accumulator use counter
+      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+        const int4 tl = p.tiles[t];
+        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t ab = it & 1, aph = (it >> 1) & 1;
+          if (!mbar_wait(acce + ab, aph ^ 1, kWaitBudgetNs) ||
+              !mbar_wait(full + stage, phase, kWaitBudgetNs)) {
+            gemm_error(p.err, 2); s_abort = 1; break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(stage_base + (size_t)stage * Cfg::STAGE_BYTES);
+          const uint32_t bh = a + Cfg::A_BYTES, bl = bh + Cfg::B_BYTES;
+          const uint32_t d = tmem + ab * BN;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bh + kk * 32), idesc,
+                       kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bl + kk * 32), idesc, 1u);
+          mma_commit(empty + stage);
+          mma_commit(accf + ab);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      // every issued MMA has retired before TMEM is released
+      if (it > 0) {
+        mma_commit(done);
+        if (!mbar_wait(done, 0, kWaitBudgetNs)) gemm_error(p.err, 3);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM lane quadrant = warp % 4, column group
+    constexpr int CPT = Cfg::CPT;
+    const int q = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * CPT;
+    const int row = q * 32 + lane;                 // weight row within the M tile
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + col0;
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+      const int4 tl = p.tiles[t];
+      const int e = tl.x, m = tl.y, row0 = tl.z;
+      const int ncount = tl.w & 0xFF;
+      const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+      float r[CPT];
+#pragma unroll
+      for (int n = 0; n < CPT; ++n) r[n] = 0.f;
+      const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const uint32_t ab = it & 1, aph = (it >> 1) & 1;
+        if (!mbar_wait(accf + ab, aph, kWaitBudgetNs)) {
+          gemm_error(p.err, 4); s_abort = 1; ok = false; break;
+        }
+        tc_fence_after();
+        const float sw = __ldg(ws + kb);
+#pragma unroll
+        for (int j = 0; j < CPT / 16; ++j) {
+          uint32_t v[16];
+          tmem_ld16(lane_base + ab * BN + j * 16, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int n = j * 16 + c;
+            const float sx = col0 + n < ncount
+                                 ? __ldg(p.xscale + (size_t)(row0 + col0 + n) * p.kblocks + kb)
+                                 : 0.f;
+            r[n] = fmaf(sw * sx, __uint_as_float(v[c]), r[n]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acce + ab);
+      }
+      if (!ok) break;
+      const int split = kb0 / p.kbps;
+      float* o = p.out + ((size_t)split * p.P + row0 + col0) * p.Mtot + m * 128 + row;
+#pragma unroll
+      for (int n = 0; n < CPT; ++n)
+        if (col0 + n < ncount) o[(size_t)n * p.Mtot] = r[n];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+template <int BN>
+static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& gp,
+                       int max_tiles, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    D3_CUDA_TRY(cudaFuncSetAttribute(moe_gemm_kernel<BN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM),
+                "gemm smem attribute");
+    attr_set[dev] = true;
+  }
+  int grid = num_sms();
+  if (max_tiles < grid) grid = max_tiles;
+  if (grid < 1) grid = 1;
+  moe_gemm_kernel<BN><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(tw, tx, gp);
+  return launch_status("moe_gemm_kernel launch");
+}
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" {
+
+size_t d3_moe_workspace_size(int32_t T, int32_t topk, int32_t n_experts, int32_t H, int32_t I) {
+  if (T < 1 || topk < 1 || n_experts < 1 || H < 128 || I < 128 || H % 128 || I % 128) return 0;
+  if ((long)T * topk > kMaxPairs) return 0;
+  Plan p;
+  make_plan(p, T, topk, n_experts, H, I, num_sms());
+  return p.total;
+}
+
+int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const void* weights,
+                       int32_t weights_f32, int32_t T, int32_t topk, const void* w13,
+                       const float* s13, const void* w2, const float* s2, int32_t n_experts,
+                       int32_t H, int32_t I, void* out, int32_t* err_word, void* workspace,
+                       size_t workspace_bytes, d3_stream_t stream) {
+  D3_CHECK_ARG(x && ids && weights && w13 && s13 && w2 && s2 && out && err_word,
+               "d3_moe_fp8_forward: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(T >= 1 && topk >= 1 && topk <= 64, "T >= 1 and 1 <= topk <= 64 required");
+  if ((long)T * topk > kMaxPairs)
+    return fail(D3_ERR_TOO_LARGE, "T*topk = %ld exceeds %d", (long)T * topk, kMaxPairs);
+  if (n_experts < 1 || n_experts > kMaxExperts)
+    return fail(D3_ERR_TOO_LARGE, "n_experts must be in [1, %d]", kMaxExperts);
+  if (H % 128 || I % 128 || H < 128 || I < 128 || H > 16384 || I > 16384)
+    return fail(D3_ERR_UNSUPPORTED, "H and I must be multiples of 128 in [128, 16384]");
+  if (!aligned16(x) || !aligned16(out) || !aligned16(w13) || !aligned16(w2))
+    return fail(D3_ERR_MISALIGNED, "x, out, w13 and w2 must be 16-byte aligned");
+  Plan pl;
+  make_plan(pl, T, topk, n_experts, H, I, num_sms());
+  if (!workspace || workspace_bytes < pl.total)
+    return fail(D3_ERR_WORKSPACE, "moe workspace needs %zu bytes (got %zu)", pl.total,
+                workspace_bytes);
+  if (!aligned16(workspace)) return fail(D3_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int P = pl.P;
+
+  RouteParams rp{};
+  rp.ids = ids; rp.ids_bytes = ids_bytes; rp.P = P; rp.n = n_experts;
+  rp.cnt = (int*)(ws + pl.o_cnt); rp.off = (int*)(ws + pl.o_off);
+  rp.sorted = (int*)(ws + pl.o_sorted); rp.inv = (int*)(ws + pl.o_inv);
+  rp.tiles1 = (int4*)(ws + pl.o_tiles1); rp.tiles2 = (int4*)(ws + pl.o_tiles2);
+  rp.ntiles = (int*)(ws + pl.o_ntiles);
+  rp.BN = pl.BN;
+  rp.mt1 = 2 * I / 128; rp.nkb1 = H / 128; rp.kbps1 = pl.kbps1; rp.split1 = pl.split1;
+  rp.mt2 = H / 128; rp.nkb2 = I / 128; rp.kbps2 = pl.kbps2; rp.split2 = pl.split2;
+  const size_t rsmem = sizeof(int) * 2 * (size_t)n_experts;
+  if (rsmem > 48 * 1024)
+    D3_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)rsmem),
+                "route smem attribute");
+  // rows of `sorted` past the valid pairs stay -1 so quant writes zeros there
+  D3_CUDA_TRY(cudaMemsetAsync(rp.sorted, 0xFF, sizeof(int) * (size_t)P, st), "memset sorted");
+  route_kernel<<<1, 1024, rsmem, st>>>(rp);
+  int rc = launch_status("route_kernel launch");
+  if (rc) return rc;
+
+  uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
+  float* xs = (float*)(ws + pl.o_xs);
+  {
+    const long warps = (long)pl.Ppad * (H / 128);
+    quant_x_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), rp.sorted, P, pl.Ppad, topk, H, xq, xs);
+    if ((rc = launch_status("quant_x_kernel launch"))) return rc;
+  }
+  CUtensorMap tw1, tx1, tw2, tx2;
+  if ((rc = make_tmap_u8(&tw1, w13, H, (uint64_t)n_experts * 2 * I, H, 128))) return rc;
+  if ((rc = make_tmap_u8(&tx1, xq, 2 * H, pl.Ppad, 2 * H, pl.BN))) return rc;
+  float* ws1 = (float*)(ws + pl.o_ws1);
+  GemmParams g1{};
+  g1.tiles = rp.tiles1; g1.ntiles = rp.ntiles; g1.wscale = s13;
+  g1.rows_per_expert = 2 * I; g1.mblocks = 2 * I / 128; g1.kblocks = H / 128;
+  g1.xscale = xs; g1.K = H; g1.out = ws1; g1.P = P; g1.Mtot = 2 * I; g1.kbps = pl.kbps1;
+  g1.err = err_word;
+  rc = pl.BN == 16 ? launch_gemm<16>(tw1, tx1, g1, pl.maxt1, st)
+                   : launch_gemm<64>(tw1, tx1, g1, pl.maxt1, st);
+  if (rc) return rc;
+
+  uint8_t* hq = (uint8_t*)(ws + pl.o_hq);
+  float* hs = (float*)(ws + pl.o_hs);
+  {
+    const long warps = (long)pl.Ppad * (I / 128);
+    act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        ws1, pl.split1, P, pl.Ppad, rp.ntiles + 2, I, hq, hs);
+    if ((rc = launch_status("act_kernel launch"))) return rc;
+  }
+  if ((rc = make_tmap_u8(&tw2, w2, I, (uint64_t)n_experts * H, I, 128))) return rc;
+  if ((rc = make_tmap_u8(&tx2, hq, 2 * I, pl.Ppad, 2 * I, pl.BN))) return rc;
+  float* ws2 = (float*)(ws + pl.o_ws2);
+  GemmParams g2{};
+  g2.tiles = rp.tiles2; g2.ntiles = rp.ntiles + 1; g2.wscale = s2;
+  g2.rows_per_expert = H; g2.mblocks = H / 128; g2.kblocks = I / 128;
+  g2.xscale = hs; g2.K = I; g2.out = ws2; g2.P = P; g2.Mtot = H; g2.kbps = pl.kbps2;
+  g2.err = err_word;
+  rc = pl.BN == 16 ? launch_gemm<16>(tw2, tx2, g2, pl.maxt2, st)
+                   : launch_gemm<64>(tw2, tx2, g2, pl.maxt2, st);
+  if (rc) return rc;
+  {
+    const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
+    combine_kernel<<<grid, 128, 0, st>>>(ws2, pl.split2, P, H, rp.inv, weights, weights_f32, T,
+                                         topk, static_cast<__nv_bfloat16*>(out));
+    if ((rc = launch_status("combine_kernel launch"))) return rc;
+  }
+  return D3_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,209 @@
+// MoE router: logits = x @ gate_w^T, softmax, top-k, renormalisation.
+//
+// Semantics of the upstream fish-speech router the reference calls into
+// (gate Linear -> softmax -> top-8 -> norm_topk_prob renorm; quoted at
+// notes/01-static-findings.md:133-138): logits are bf16, the softmax runs in
+// fp32, ties in the top-k go to the lower expert index.  Expert ids must be
+// bit-exact, so every logit is the EXACTLY ROUNDED bf16 of the dot product:
+// the bf16 x bf16 products are exact in fp64 and accumulate in fp64 (error
+// ~1e-16 relative, far below a bf16 ulp), then round to fp32 and to bf16,
+// both round-to-nearest-even.  Any other accumulation order only changes the
+// fp64 sum's last bits, so every correct implementation agrees on the ids.
+//
+// Kernel shape: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one
+// expert per warp over a tile of 8 tokens staged in shared memory (each gate
+// row is read once per token tile).  The last CTA of a token tile to finish
+// (a global arrival counter, reset by that CTA for the next launch or graph
+// replay) selects the top-k of its tokens: one warp per token, 8 logits per
+// lane for E = 256, k rounds of a warp arg-max.
+#include "d3_common.cuh"
+
+#include <cuda_bf16.h>
+
+namespace d3 {
+
+constexpr int kRouterExpertsPerCta = 8;   // one per warp
+constexpr int kRouterTokensPerCta = 8;
+constexpr int kRouterMaxH = 8192;
+constexpr int kRouterMaxE = 1024;
+
+struct RouterParams {
+  const __nv_bfloat16* x;     // [T, H]
+  const __nv_bfloat16* w;     // [E, H]
+  int32_t T, H, E, topk, renorm;
+  float* logits;              // workspace [T, E] (bf16 values held in fp32)
+  unsigned int* arrivals;     // workspace [ceil(T/8)], zero between launches
+  int32_t* ids_out;           // [T, topk]
+  float* weights_out;         // [T, topk] or null
+  __nv_bfloat16* weights_bf16_out;  // [T, topk] or null
+};
+
+__device__ __forceinline__ float exact_bf16_of(double s) {
+  return __bfloat162float(__float2bfloat16_rn(__double2float_rn(s)));
+}
+
+__global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
+  __shared__ bool s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * kRouterTokensPerCta;
+  const int nt = min(kRouterTokensPerCta, p.T - t0);
+  // stage the token tile (16-byte vectors; H % 8 == 0 is checked on the host)
+  const int vec_per_row = p.H / 8;
+  for (int i = threadIdx.x; i < nt * vec_per_row; i += blockDim.x) {
+    const int r = i / vec_per_row, c = i - r * vec_per_row;
+    reinterpret_cast<uint4*>(xs)[r * vec_per_row + c] =
+        reinterpret_cast<const uint4*>(p.x + (size_t)(t0 + r) * p.H)[c];
+  }
+  __syncthreads();
+  const int e = blockIdx.x * kRouterExpertsPerCta + warp;
+  if (e < p.E) {
+    double acc[kRouterTokensPerCta];
+#pragma unroll
+    for (int t = 0; t < kRouterTokensPerCta; ++t) acc[t] = 0.0;
+    const uint4* wrow = reinterpret_cast<const uint4*>(p.w + (size_t)e * p.H);
+    for (int c = lane; c < vec_per_row; c += 32) {
+      const uint4 wv = __ldg(wrow + c);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      double wd[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) wd[q] = (double)__bfloat162float(wb[q]);
+#pragma unroll
+      for (int t = 0; t < kRouterTokensPerCta; ++t) {
+        if (t < nt) {
+          const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
+          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[t] = fma((double)__bfloat162float(xb[q]), wd[q], acc[t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterTokensPerCta; ++t) {
+      double v = acc[t];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0 && t < nt) p.logits[(size_t)(t0 + t) * p.E + e] = exact_bf16_of(v);
+    }
+  }
+  // last CTA of this token tile does the selection
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(p.arrivals + blockIdx.y, 1u);
+    s_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (warp < nt) {
+    const int t = t0 + warp;
+    const float* lg = p.logits + (size_t)t * p.E;
+    constexpr int kPer = kRouterMaxE / 32;
+    float v[kPer];
+    const int per = (p.E + 31) / 32;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = j * 32 + lane;
+      v[j] = (j < per && i < p.E) ? __ldcg(lg + i) : -INFINITY;
+      mx = fmaxf(mx, v[j]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float denom = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per && j * 32 + lane < p.E) denom += expf(v[j] - mx);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) denom += __shfl_xor_sync(0xffffffffu, denom, off);
+    float sel_w = 0.f, sel_sum = 0.f;
+    int sel_id = -1;
+    for (int r = 0; r < p.topk; ++r) {
+      // arg-max with lower index winning ties
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int i = j * 32 + lane;
+        if (j < per && i < p.E && (v[j] > bv || (v[j] == bv && i < bi))) { bv = v[j]; bi = i; }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      const float pr = expf(bv - mx) / denom;
+      if (lane == r) { sel_id = bi; sel_w = pr; }
+      sel_sum += pr;
+      // remove the winner
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (j * 32 + lane == bi) v[j] = -INFINITY;
+    }
+    if (lane < p.topk) {
+      const float wgt = p.renorm ? sel_w / sel_sum : sel_w;
+      p.ids_out[(size_t)t * p.topk + lane] = sel_id;
+      if (p.weights_out) p.weights_out[(size_t)t * p.topk + lane] = wgt;
+      if (p.weights_bf16_out) p.weights_bf16_out[(size_t)t * p.topk + lane] = __float2bfloat16_rn(wgt);
+    }
+  }
+  if (threadIdx.x == 0) p.arrivals[blockIdx.y] = 0;  // ready for the next launch / replay
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" {
+
+size_t d3_router_workspace_size(int32_t T, int32_t E) {
+  if (T <= 0 || E <= 0) return 0;
+  const size_t tiles = (size_t)(T + kRouterTokensPerCta - 1) / kRouterTokensPerCta;
+  return align256((size_t)T * E * sizeof(float)) + align256(tiles * sizeof(unsigned));
+}
+
+int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int32_t E,
+                   int32_t topk, int32_t renorm, int32_t* ids_out, float* weights_out,
+                   void* weights_bf16_out, void* workspace, size_t workspace_bytes,
+                   d3_stream_t stream) {
+  D3_CHECK_ARG(x && gate_w && ids_out, "d3_router_topk: null pointer");
+  D3_CHECK_ARG(T >= 1, "T must be >= 1");
+  D3_CHECK_ARG(H >= 8 && H % 8 == 0 && H <= kRouterMaxH, "H must be a multiple of 8 in [8, %d]",
+               kRouterMaxH);
+  D3_CHECK_ARG(E >= 1 && E <= kRouterMaxE, "E must be in [1, %d]", kRouterMaxE);
+  D3_CHECK_ARG(topk >= 1 && topk <= 32 && topk <= E, "topk must be in [1, min(32, E)]");
+  if (!aligned16(x) || !aligned16(gate_w))
+    return fail(D3_ERR_MISALIGNED, "x and gate_w must be 16-byte aligned");
+  const size_t need = d3_router_workspace_size(T, E);
+  if (!workspace || workspace_bytes < need)
+    return fail(D3_ERR_WORKSPACE, "router workspace needs %zu bytes (got %zu)", need,
+                workspace_bytes);
+  // The arrival counters start at zero (the caller zero-fills the workspace
+  // once) and every launch leaves them at zero again.
+  RouterParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.w = static_cast<const __nv_bfloat16*>(gate_w);
+  p.T = T; p.H = H; p.E = E; p.topk = topk; p.renorm = renorm;
+  p.logits = static_cast<float*>(workspace);
+  p.arrivals = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) +
+                                           align256((size_t)T * E * sizeof(float)));
+  p.ids_out = ids_out;
+  p.weights_out = weights_out;
+  p.weights_bf16_out = static_cast<__nv_bfloat16*>(weights_bf16_out);
+  const dim3 grid((unsigned)((E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
+                  (unsigned)((T + kRouterTokensPerCta - 1) / kRouterTokensPerCta));
+  const size_t smem = (size_t)kRouterTokensPerCta * H * sizeof(__nv_bfloat16);
+  if (smem > 48 * 1024)
+    D3_CUDA_TRY(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "router smem attribute");
+  router_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(p);
+  return launch_status("router_kernel launch");
+}
+
+}  // extern "C"

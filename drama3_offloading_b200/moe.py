@@ -1,0 +1,121 @@
+"""Router and FP8 expert computation -- the calls the reference makes into
+upstream fish-speech, served by libd3b200.so.
+
+* ``router_topk(x, gate_w, k, renorm)`` -- the MoE block's gate -> softmax ->
+  top-k -> renorm (fish-speech moe.py:217-220, quoted in the reference at
+  notes/01-static-findings.md:133-138).
+* ``fp8_moe_forward(x, ids, w, w13, s13, w2, s2)`` -- same signature and
+  meaning as upstream ``fp8_moe_forward`` as the reference calls it
+  (bin/devcache.py:275-277, bin/offload.py:177, :239, :340, :388, :449):
+  ``ids`` index dim 0 of the weight stacks (expert ids, cache slots or a
+  renumbered subset), ``w`` are the routing weights, the result is bf16.
+
+Workspaces are allocated once per (device, size) and reused, so repeated
+calls -- and CUDA-graph capture -- do not allocate.  Kernel-side failures
+(a bounded wait that timed out) set a device error word instead of hanging;
+``check_errors()`` reads it (synchronising).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_WS: dict = {}
+_ERR: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int, tag: str, zero: bool = False) -> torch.Tensor:
+    key = (tag, device.index)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    t = _ERR.get(device.index)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[device.index] = t
+    return t
+
+
+def check_errors(device=None) -> None:
+    """Raise if any GEMM on ``device`` gave up on a bounded wait."""
+    device = torch.device(device or torch.cuda.current_device())
+    if device.type != "cuda":
+        device = torch.device("cuda", torch.cuda.current_device())
+    v = int(error_word(device).item())
+    if v:
+        raise RuntimeError(f"d3 MoE GEMM reported device error code {v} (a bounded wait expired)")
+
+
+def router_topk(x: torch.Tensor, gate_w: torch.Tensor, k: int = 8, renorm: bool = True,
+                out_ids: torch.Tensor | None = None, out_w: torch.Tensor | None = None,
+                out_w_bf16: torch.Tensor | None = None, stream=None):
+    """x bf16 [T,H], gate_w bf16 [E,H] -> (ids int32 [T,k], weights f32 [T,k])."""
+    if x.dtype != torch.bfloat16 or gate_w.dtype != torch.bfloat16:
+        raise TypeError("router_topk expects bf16 x and gate_w")
+    x = x.contiguous()
+    gate_w = gate_w.contiguous()
+    T, H = x.shape
+    E = gate_w.shape[0]
+    dev = x.device
+    ids = out_ids if out_ids is not None else torch.empty(T, k, dtype=torch.int32, device=dev)
+    w = out_w if out_w is not None else torch.empty(T, k, dtype=torch.float32, device=dev)
+    need = _lib.load().d3_router_workspace_size(T, E)
+    ws = _workspace(dev, need, "router")
+    _lib.call("d3_router_topk", _lib.ptr(x), _lib.ptr(gate_w), T, H, E, k, 1 if renorm else 0,
+              _lib.ptr(ids), _lib.ptr(w), _lib.ptr(out_w_bf16), _lib.ptr(ws), ws.numel(),
+              _lib.stream_ptr(stream))
+    return ids, w
+
+
+def workspace_bytes(T: int, topk: int, n_experts: int, H: int, I: int) -> int:
+    return int(_lib.load().d3_moe_workspace_size(T, topk, n_experts, H, I))
+
+
+def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                    w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+                    out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Routed MoE over block-scaled FP8 experts; returns bf16 [T, H].
+
+    ids (int32/int64) out of range -- e.g. -1 -- contribute nothing."""
+    if x.dtype != torch.bfloat16:
+        raise TypeError("x must be bf16")
+    x = x.contiguous()
+    T, H = x.shape
+    ids = ids.reshape(T, -1)
+    topk = ids.shape[1]
+    if ids.dtype not in (torch.int32, torch.int64):
+        ids = ids.to(torch.int32)
+    ids = ids.contiguous()
+    weights = weights.reshape(T, topk)
+    if weights.dtype not in (torch.float32, torch.bfloat16):
+        weights = weights.to(torch.float32)
+    weights = weights.contiguous()
+    n, two_i, h2 = w13.shape
+    if h2 != H or w2.shape[0] != n or w2.shape[1] != H:
+        raise ValueError("weight shapes do not match x")
+    I = two_i // 2
+    for t, name in ((w13, "w13"), (w2, "w2")):
+        if t.element_size() != 1 or not t.is_contiguous():
+            raise TypeError(f"{name} must be a contiguous 1-byte (e4m3) tensor")
+    s13 = s13.contiguous()
+    s2 = s2.contiguous()
+    if s13.dtype != torch.float32 or s2.dtype != torch.float32:
+        raise TypeError("scales must be float32")
+    dev = x.device
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    need = workspace_bytes(T, topk, n, H, I)
+    if need == 0:
+        raise ValueError(f"unsupported MoE shape T={T} topk={topk} n={n} H={H} I={I}")
+    ws = _workspace(dev, need, "moe")
+    _lib.call("d3_moe_fp8_forward", _lib.ptr(x), _lib.ptr(ids), ids.element_size(),
+              _lib.ptr(weights), 1 if weights.dtype == torch.float32 else 0, T, topk,
+              _lib.ptr(w13), _lib.ptr(s13), _lib.ptr(w2), _lib.ptr(s2), n, H, I, _lib.ptr(out),
+              _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(), _lib.stream_ptr(stream))
+    return out

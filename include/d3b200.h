@@ -139,6 +139,52 @@ D3_API int d3_fetch_jobs(const d3_layer_cache* layer, int32_t fetch_ctas, d3_str
 D3_API int d3_lookup_slots(const int32_t* slot_of, int32_t num_experts, const void* ids,
                     int32_t ids_bytes, int32_t n, int32_t* slot_out, d3_stream_t stream);
 
+/* ------------------------------------------------------------------ router */
+
+/* Workspace bytes d3_router_topk needs for T tokens and E experts. */
+D3_API size_t d3_router_workspace_size(int32_t T, int32_t E);
+
+/* MoE router: logits = x @ gate_w^T (bf16 [T,H] x bf16 [E,H]), softmax over E,
+ * top-k (ties -> lower expert index), weights renormalised over the k when
+ * renorm != 0.  Logits are the exactly rounded bf16 of each dot product.
+ * Outputs: ids_out int32 [T,k]; weights_out f32 [T,k] and/or
+ * weights_bf16_out bf16 [T,k] (either may be NULL).  The workspace must be
+ * zero-filled once before its first use (every call leaves it reusable).
+ * Limits: H % 8 == 0, H <= 8192, E <= 1024, k <= 32.
+ * Replaces the upstream MoE block's gate -> softmax -> topk -> renorm
+ * (fish-speech moe.py:217-220, quoted at notes/01-static-findings.md:133-138),
+ * whose topk_ids feed dev_cached_forward -- bin/devcache.py:258-277. */
+D3_API int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int32_t E,
+                          int32_t topk, int32_t renorm, int32_t* ids_out, float* weights_out,
+                          void* weights_bf16_out, void* workspace, size_t workspace_bytes,
+                          d3_stream_t stream);
+
+/* ------------------------------------------------------------- expert GEMM */
+
+/* Workspace bytes d3_moe_fp8_forward needs (0 = unsupported shape). */
+D3_API size_t d3_moe_workspace_size(int32_t T, int32_t topk, int32_t n_experts, int32_t H,
+                                    int32_t I);
+
+/* Routed MoE over block-scaled FP8 experts.  For every pair (t, j) with
+ * e = ids[t,j] in [0, n_experts):
+ *   h = silu(x_t Wg[e]^T) * (x_t Wu[e]^T),   out_t += weights[t,j] * h Wd[e]^T
+ * x bf16 [T,H]; ids int32/int64 [T,topk] (ids_bytes 4/8; out-of-range ids are
+ * skipped); weights f32 (weights_f32 = 1) or bf16 [T,topk]; w13 e4m3 [n,2I,H]
+ * (gate rows [0,I), up rows [I,2I)), s13 f32 [n,2I/128,H/128]; w2 e4m3 [n,H,I],
+ * s2 f32 [n,H/128,I/128] (weight = byte x scale of its 128x128 block);
+ * out bf16 [T,H].  err_word: device int32, set non-zero (never cleared) if a
+ * kernel gave up on a bounded wait.  Limits: H, I multiples of 128 in
+ * [128, 16384]; T*topk <= 65536; n_experts <= 8192.
+ * Replaces upstream fp8_moe_forward(x, ids, w, w13, s13, w2, s2) as called by
+ * dev_cached_forward -- bin/devcache.py:275-277 -- and the gather paths --
+ * bin/offload.py:177, :239, :340, :388, :449. */
+D3_API int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes,
+                              const void* weights, int32_t weights_f32, int32_t T, int32_t topk,
+                              const void* w13, const float* s13, const void* w2, const float* s2,
+                              int32_t n_experts, int32_t H, int32_t I, void* out,
+                              int32_t* err_word, void* workspace, size_t workspace_bytes,
+                              d3_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
