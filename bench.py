@@ -1,19 +1,23 @@
 """Benchmark of the routed-MoE expert-offload hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|fetch]
+                    [--impl ours|reference]
 
 Workloads:
 
-* ``fetch``  -- configs[1], the expert-fetch microbenchmark: 40 layers x 256
-  experts of FP8 weights + scales (30 GiB) in pinned host memory, per-layer
-  device caches totalling 2048 slots (51 per layer), the synthetic Zipf(1.1)
-  routing trace (top-8 per layer), one decode step = 40 x (allocator + fused
-  fetch) replayed from a CUDA graph.  Metric: fetch GB/s vs the measured
-  host-link (pinned copy-engine) peak.
+* ``decode`` (default) -- configs[2]: 40-layer Drama-3-shaped MoE decode,
+  batch 1, random init (hidden 2048, 256 experts, top-8, FP8 experts + 6.9 GiB
+  of bf16 dense weights read per token), experts offloaded to pinned host
+  memory with an 8 GiB device cache (68 slots per layer), routing from the
+  seeded Zipf(1.1) trace.  One step = one token through all 40 layers, replayed
+  from a CUDA graph.  Metric: decode tok/s; the fetch kernel's host-link GB/s
+  against the measured pinned copy-engine peak is reported beside it.
+* ``fetch`` -- configs[1]: the expert-fetch microbenchmark (40 x 256 experts
+  pinned, 2048 slots in total, graph-captured allocator + fetch per layer).
 
-A step is one decode step over all 40 layers.  Inputs (the 30 GiB host store)
-are far larger than L2.  Multi-GPU runs are replicas (each rank its own store
-and link; "scaling": "weak").
+Inputs are far larger than L2 (30 GiB host store, 6.9 GiB dense weights, 8 GiB
+cache).  Multi-GPU runs are replicas (each rank its own store, cache and host
+link; "scaling": "weak"), timed on the device, max over ranks.
 """
 from __future__ import annotations
 
@@ -30,6 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 EXPERT_BYTES = 3_146_496
+METRIC_DECODE = "decode tok/s (40L, bs1, offloaded) + expert-fetch GB/s vs host-link peak"
+METRIC_FETCH = "expert-fetch GB/s (40L x 256 experts pinned, 2048-slot cache, Zipf(1.1), graph)"
 
 
 def parse():
@@ -38,13 +44,16 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("fetch",), default="fetch")
+    ap.add_argument("--workload", choices=("decode", "fetch"), default="decode")
     ap.add_argument("--layers", type=int, default=40)
-    ap.add_argument("--slots", type=int, default=2048, help="device cache slots over all layers")
+    ap.add_argument("--slots", type=int, default=2048, help="fetch workload: slots over all layers")
+    ap.add_argument("--cache-gib", type=float, default=8.0, help="decode workload device cache")
     ap.add_argument("--policy", choices=("lru", "lfu"), default="lru")
     ap.add_argument("--fetch-ctas", type=int, default=0)
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
+    ap.add_argument("--cpu-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
     return ap.parse_args()
 
 
@@ -52,41 +61,188 @@ def init_dist(args):
     from drama3_offloading_b200.benchutil import dist_env
     rank, world, local = dist_env()
     if world > 1:
-        import torch.distributed as dist
-        if args.impl == "ours" or torch.cuda.is_available():
-            torch.cuda.set_device(local)
         import datetime
+        import torch.distributed as dist
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
         dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
                                 timeout=datetime.timedelta(seconds=600))
     return rank, world, local
 
 
-# ---------------------------------------------------------------- CPU legs
+# ---------------------------------------------------------------- CPU legs (oracle)
 
-def cpu_fetch_baseline(trace: np.ndarray, capacity: int, policy: str, sample_s: float) -> dict:
-    """The oracle's allocator plus a memcpy of every missed expert (host store
-    -> host cache), timed on this box's cores over a bounded sample of the
-    same trace.  One thread (the reference's allocator and fetch are serial)."""
+class CpuDecodeSample:
+    """``layers`` CPU layers of the decode stack: torch bf16 dense GEMVs, the
+    oracle router, the oracle LRU allocator, a memcpy of each missed expert
+    into a host-side cache, and the oracle's dequantise-then-matmul experts
+    (the reference's torch CPU MoE path).  A bounded sample of the 40 layers."""
+
+    def __init__(self, layers, trace, capacity, hidden=2048, inter=512, experts=256, R=22528,
+                 seed=0):
+        import oracle
+        from drama3_offloading_b200 import synth
+        self.o = oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.threads = torch.get_num_threads()
+        gen = "cuda" if torch.cuda.is_available() else "cpu"
+        g = torch.Generator().manual_seed(seed + 7)
+        self.L, self.k, self.trace = layers, trace.shape[2], trace
+        self.ex = [synth.make_experts(experts, hidden, inter, seed=seed + l, device=gen,
+                                      chunk=32).to("cpu") for l in range(layers)]
+        self.up = [(torch.randn(R, hidden, generator=g) * hidden ** -0.5).to(torch.bfloat16)
+                   for _ in range(layers)]
+        self.down = [(torch.randn(hidden, R, generator=g) * (R ** -0.5 * 0.5)).to(torch.bfloat16)
+                     for _ in range(layers)]
+        self.gate = [(torch.randn(experts, hidden, generator=g) * 0.02).to(torch.bfloat16)
+                     for _ in range(layers)]
+        self.tabs = [oracle.init_tables(experts, capacity) for _ in range(layers)]
+        self.c13 = [torch.zeros((capacity, 2 * inter, hidden), dtype=torch.float8_e4m3fn)
+                    for _ in range(layers)]
+        self.c2 = [torch.zeros((capacity, hidden, inter), dtype=torch.float8_e4m3fn)
+                   for _ in range(layers)]
+        self.s13 = [torch.ones(capacity, 2 * inter // 128, hidden // 128) for _ in range(layers)]
+        self.s2 = [torch.ones(capacity, hidden // 128, inter // 128) for _ in range(layers)]
+        self.h = torch.randn(1, hidden, generator=g).to(torch.bfloat16)
+        self.pos = 0
+
+    def token(self) -> float:
+        o = self.o
+        t0 = time.perf_counter()
+        row = self.trace[self.pos % self.trace.shape[0]]
+        for l in range(self.L):
+            h = self.h
+            h = h + torch.nn.functional.silu(h @ self.up[l].t()) @ self.down[l].t()
+            _, w, _, _ = o.router_topk(h, self.gate[l], self.k)
+            slots, fs, fe, n = o.resolve(self.tabs[l], row[l])
+            ex = self.ex[l]
+            for j in range(n):
+                s, e = int(fs[j]), int(fe[j])
+                self.c13[l][s].copy_(ex.w13_weight[e])
+                self.c2[l][s].copy_(ex.w2_weight[e])
+                self.s13[l][s].copy_(ex.w13_scale_inv[e])
+                self.s2[l][s].copy_(ex.w2_scale_inv[e])
+            y = o.moe_forward(h, torch.from_numpy(slots.astype(np.int64)).reshape(1, -1), w,
+                              self.c13[l], self.s13[l], self.c2[l], self.s2[l])
+            y = h.float() + y
+            y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6)
+            self.h = y.to(torch.bfloat16)
+        self.pos += 1
+        return time.perf_counter() - t0
+
+
+def cpu_decode_baseline(trace, capacity, layers_total, sample_layers, sample_s) -> dict:
+    cpu = CpuDecodeSample(sample_layers, trace, capacity)
+    cpu.token()  # warm
+    t0 = time.perf_counter()
+    times = []
+    while time.perf_counter() - t0 < sample_s or not times:
+        times.append(cpu.token())
+    per_layer = float(np.mean(times)) / sample_layers
+    return {"value": 1.0 / (per_layer * layers_total), "unit": "tok/s", "cores": cpu.threads,
+            "kind": "port",
+            "sample": f"{len(times)} tokens x {sample_layers} of {layers_total} layers (per-token "
+                      f"time scaled by {layers_total}/{sample_layers}); torch bf16 dense GEMVs + "
+                      f"oracle router/LRU + expert memcpy + dequantised fp32 expert matmuls"}
+
+
+def cpu_fetch_baseline(trace, capacity, sample_s) -> dict:
+    """The oracle allocator + a memcpy of every missed expert (host store ->
+    host cache), one thread, over a bounded prefix of the trace."""
     import oracle
     layers = trace.shape[1]
     store = np.random.default_rng(0).integers(0, 255, size=(16, EXPERT_BYTES), dtype=np.uint8)
     cache = np.zeros((capacity, EXPERT_BYTES), dtype=np.uint8)
     tabs = [oracle.init_tables(256, capacity) for _ in range(layers)]
-    res = oracle.resolve_lfu if policy == "lfu" else oracle.resolve
     t0 = time.perf_counter()
     steps = misses = 0
     while time.perf_counter() - t0 < sample_s and steps < trace.shape[0]:
         for l in range(layers):
-            _, fs, fe, n = res(tabs[l], trace[steps, l])
+            _, fs, fe, n = oracle.resolve(tabs[l], trace[steps, l])
             for j in range(n):
                 cache[fs[j]] = store[int(fe[j]) % 16]
             misses += n
         steps += 1
     dt = time.perf_counter() - t0
     return {"value": misses * EXPERT_BYTES / dt / 1e9, "unit": "GB/s", "cores": 1,
-            "kind": "port", "steps": steps, "seconds": dt,
-            "sample": f"first {steps} steps x {layers} layers of the Zipf trace, LRU oracle + "
-                      f"memcpy of each missed 3,146,496-B expert (host->host)"}
+            "kind": "port",
+            "sample": f"first {steps} steps x {layers} layers of the Zipf trace: LRU oracle + memcpy "
+                      f"of each missed 3,146,496-B expert (host->host)"}
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- decode (configs[2])
+
+def run_decode(args, rank, world, local):
+    from drama3_offloading_b200 import benchutil
+    from drama3_offloading_b200.decode import DecodeStack
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peak = benchutil.host_link_peak_gbs(device=dev)
+    stack = DecodeStack(layers=args.layers, cache_gib=args.cache_gib, device=dev,
+                        policy=args.policy)
+    from drama3_offloading_b200 import devcache
+    devcache.FETCH_CTAS = args.fetch_ctas
+    g = stack.capture()
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    c0 = stack.store.counters()
+    benchutil.barrier(world, dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with benchutil.ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        a.record()
+        for _ in range(args.steps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+    benchutil.barrier(world, dev)
+    ms = a.elapsed_time(b)
+    c1 = stack.store.counters()
+    misses = (c1["misses"] - c0["misses"]) / args.steps
+    hits = (c1["hits"] - c0["hits"]) / args.steps
+    ms_max = benchutil.max_over_ranks(ms, world, dev)
+    value = world * args.steps / (ms_max * 1e-3)
+
+    # end to end through the public API: per token, the input hidden state
+    # comes from pinned host memory and the output goes back to it
+    h_in = torch.randn(1, stack.H, dtype=torch.bfloat16).pin_memory()
+    h_out = torch.empty(1, stack.H, dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize(dev)
+    benchutil.barrier(world, dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        stack.h.copy_(h_in, non_blocking=True)
+        g.replay()
+        h_out.copy_(stack.h, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = benchutil.max_over_ranks(e0.elapsed_time(e1), world, dev)
+    e2e = world * args.e2e_steps / (e2e_ms * 1e-3)
+
+    # fetch kernel bandwidth, measured with events around every layer's
+    # allocator+fetch launch pair over a few eager steps
+    ft = stack.sample_fetch_timing(8)
+    fetch_gbs = ft["bytes"] / (ft["ms"] * 1e-3) / 1e9 if ft["ms"] > 0 else 0.0
+    hbm = measured_peaks()
+    roof_ms = stack.roofline_ms(hits, misses, hbm["hbm_gbs"], peak["gbs"])
+    return {"value": value, "ms": ms_max, "e2e": e2e, "clk": clk.summary(), "peak": peak,
+            "hits": hits, "misses": misses, "fetch_gbs": fetch_gbs, "fetch_sample": ft,
+            "roof_ms": roof_ms, "hbm": hbm, "capacity": stack.capacity,
+            "launches": stack.launches_per_step() * args.steps, "trace": stack.trace_dev.cpu().numpy(),
+            "dense_bytes": stack.dense_bytes}
 
 
 # ---------------------------------------------------------------- fetch (configs[1])
@@ -119,9 +275,6 @@ def run_fetch(args, rank, world, local):
     with torch.cuda.stream(s):
         one_step()
     torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize(dev)
-    # capture one step (capture executes nothing), then restart the trace and
-    # the caches cold in place so the replays start from the init state
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         one_step()
@@ -148,67 +301,118 @@ def run_fetch(args, rank, world, local):
     hits = c1["hits"] - c0["hits"]
     fetched = c1["bytes_fetched"] - c0["bytes_fetched"]
     ms_max = benchutil.max_over_ranks(ms, world, dev)
-    gbs_rank = fetched / (ms * 1e-3) / 1e9
     total_bytes = benchutil.sum_over_ranks(fetched, world, dev)
-    value = total_bytes / (ms_max * 1e-3) / 1e9
-    return {
-        "value": value, "ms": ms_max, "gbs_rank": gbs_rank, "peak": peak, "clk": clk.summary(),
-        "hit_rate": hits / max(1, hits + misses), "misses_per_step": misses / args.steps,
-        "capacity": capacity, "setup_s": store.setup_s, "trace": trace,
-        "launches": args.steps * args.layers * 2,
-    }
+    return {"value": total_bytes / (ms_max * 1e-3) / 1e9, "ms": ms_max,
+            "gbs_rank": fetched / (ms * 1e-3) / 1e9, "peak": peak, "clk": clk.summary(),
+            "hit_rate": hits / max(1, hits + misses), "misses_per_step": misses / args.steps,
+            "capacity": capacity, "trace": trace, "launches": args.steps * args.layers * 2}
+
+
+# ---------------------------------------------------------------- main
+
+def reference_arm(args, rank):
+    """--impl reference: the reference's CPU path (oracle port) on this box's
+    host cores, rank 0 only, one bounded sample per step."""
+    if rank != 0:
+        return
+    from drama3_offloading_b200.trace import zipf_trace
+    trace = zipf_trace(steps=4096, layers=args.layers)
+    if args.workload == "fetch":
+        cap = max(1, args.slots // args.layers)
+        per = max(0.05, args.cpu_sample_s / max(1, args.steps + args.warmup))
+        res = [cpu_fetch_baseline(trace, cap, per) for _ in range(args.warmup + args.steps)]
+        v = float(np.mean([r["value"] for r in res[args.warmup:]]))
+        unit, metric, dtype, r = "GB/s", METRIC_FETCH, "u8", res[-1]
+        cfg = {"workload": "fetch", "layers": args.layers, "slots": args.slots}
+    else:
+        cap = max(1, int(args.cache_gib * (1 << 30)) // (args.layers * EXPERT_BYTES))
+        cpu = CpuDecodeSample(1, trace, cap)
+        for _ in range(args.warmup):
+            cpu.token()
+        ts = [cpu.token() for _ in range(args.steps)]
+        v = 1.0 / (float(np.mean(ts)) * args.layers)
+        unit, metric, dtype = "tok/s", METRIC_DECODE, "bf16/fp8"
+        r = {"cores": cpu.threads, "kind": "port",
+             "sample": f"each step: one token through 1 of {args.layers} layers (time x "
+                       f"{args.layers}); torch bf16 dense GEMVs + oracle router/LRU + expert "
+                       f"memcpy + dequantised fp32 expert matmuls"}
+        cfg = {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
+               "cache_gib": args.cache_gib}
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": unit, "cores": r["cores"], "kind": r["kind"],
+                             "sample": r["sample"]},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def main():
     args = parse()
     rank, world, local = init_dist(args)
     if args.impl == "reference":
-        if rank != 0:
-            return
-        from drama3_offloading_b200.trace import zipf_trace
-        trace = zipf_trace(steps=4096, layers=args.layers)
-        capacity = max(1, args.slots // args.layers)
-        res = []
-        for _ in range(args.warmup + args.steps):
-            res.append(cpu_fetch_baseline(trace, capacity, args.policy,
-                                          args.cpu_sample_s / max(1, args.steps)))
-        r = res[-1]
-        v = float(np.mean([x["value"] for x in res[args.warmup:]]))
-        line = {"impl": "reference", "metric": "expert-fetch GB/s (40L, 2048-slot cache, Zipf(1.1))",
-                "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-                "config": {"workload": "fetch", "layers": args.layers, "slots": args.slots},
-                "cpu_baseline": {k: r[k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
-                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        reference_arm(args, rank)
         return
-
-    r = run_fetch(args, rank, world, local)
+    if args.workload == "fetch":
+        r = run_fetch(args, rank, world, local)
+    else:
+        r = run_decode(args, rank, world, local)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_fetch_baseline(r["trace"], r["capacity"], args.policy, args.cpu_sample_s)
+            if args.workload == "fetch":
+                cpu = cpu_fetch_baseline(r["trace"], r["capacity"], args.cpu_sample_s)
+            else:
+                cpu = cpu_decode_baseline(r["trace"], r["capacity"], args.layers, args.cpu_layers,
+                                          args.cpu_sample_s)
         peak = r["peak"]["gbs"]
-        line = {
-            "metric": "expert-fetch GB/s (40L x 256 experts pinned, 2048-slot cache, Zipf(1.1), graph)",
-            "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic (random N(0,0.02) FP8 weights, seeded Zipf(1.1) trace)",
-            "config": {"workload": "fetch", "layers": args.layers, "experts": 256,
-                       "slots": args.slots, "slots_per_layer": r["capacity"],
-                       "policy": args.policy, "l2": "inputs (30 GiB host store) > L2",
-                       "parallelism": f"replicas{world}"},
-            "hit_rate": r["hit_rate"], "misses_per_step": r["misses_per_step"],
-            "host_link_peak_gbs": peak,
-            "roofline": {"bound": "host_link", "achieved": r["gbs_rank"], "peak": peak,
-                         "unit": "GB/s", "frac": r["gbs_rank"] / peak, "traffic": None},
-            "clocks": r["clk"], "gpu_launches": r["launches"],
-            "cpu_baseline": None if cpu is None else {k: cpu[k] for k in (
-                "value", "unit", "cores", "kind", "sample")},
-        }
+        if args.workload == "fetch":
+            line = {
+                "metric": METRIC_FETCH, "value": r["value"], "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+                "data": "synthetic (random N(0,0.02) FP8 weights, seeded Zipf(1.1) trace)",
+                "config": {"workload": "expert-fetch", "layers": args.layers, "experts": 256,
+                           "slots": args.slots, "slots_per_layer": r["capacity"],
+                           "policy": args.policy, "l2": "inputs (30 GiB host store) > L2",
+                           "parallelism": f"replicas{world}"},
+                "hit_rate": r["hit_rate"], "misses_per_step": r["misses_per_step"],
+                "host_link_peak_gbs": peak,
+                "roofline": {"bound": "host_link", "achieved": r["gbs_rank"], "peak": peak,
+                             "unit": "GB/s", "frac": r["gbs_rank"] / peak, "traffic": None},
+                "clocks": r["clk"], "gpu_launches": r["launches"],
+            }
+        else:
+            tokb = r["value"] / world
+            line = {
+                "metric": METRIC_DECODE, "value": r["value"], "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "fp8 weights x (bf16-class hi/lo fp8 activations), bf16 dense",
+                "data": "synthetic (random-init Drama-3 shapes, seeded Zipf(1.1) routing trace)",
+                "config": {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
+                           "hidden": 2048, "experts": 256, "topk": 8, "cache_gib": args.cache_gib,
+                           "slots_per_layer": r["capacity"], "policy": args.policy,
+                           "dense_gib_per_token": r["dense_bytes"] / 2**30,
+                           "l2": "inputs > L2 (30 GiB host store, 6.9 GiB dense, 8 GiB cache)",
+                           "parallelism": f"replicas{world}"},
+                "hits_per_token": r["hits"], "misses_per_token": r["misses"],
+                "hit_rate": r["hits"] / max(1e-9, r["hits"] + r["misses"]),
+                "fetch_gbs": r["fetch_gbs"], "host_link_peak_gbs": peak,
+                "fetch_frac_of_host_peak": r["fetch_gbs"] / peak,
+                "token_roofline_ms": r["roof_ms"],
+                "token_roofline_frac": r["roof_ms"] / (1e3 / tokb),
+                "roofline": {"bound": "host_link", "kernel": "fetch_layer_kernel (+allocator)",
+                             "achieved": r["fetch_gbs"], "peak": peak, "unit": "GB/s",
+                             "frac": r["fetch_gbs"] / peak, "traffic": None,
+                             "peak_source": "measured pinned copy-engine H2D, this run"},
+                "e2e": {"value": r["e2e"], "unit": "tok/s", "h2d_bytes_per_step": 2 * 2048,
+                        "d2h_bytes_per_step": 2 * 2048},
+                "clocks": r["clk"], "gpu_launches": r["launches"],
+            }
+        line["cpu_baseline"] = None if cpu is None else {
+            k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

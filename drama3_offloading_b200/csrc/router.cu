@@ -26,6 +26,13 @@ constexpr int kRouterExpertsPerCta = 8;   // one per warp
 constexpr int kRouterTokensPerCta = 8;
 constexpr int kRouterMaxH = 8192;
 constexpr int kRouterMaxE = 1024;
+constexpr int kRouterMaxT = 65536;
+// Workspace layout: the per-token-tile arrival counters live at a FIXED offset
+// 0 (room for kRouterMaxT tokens), the logits after them, so a workspace
+// reused across calls with different T never finds stale logits where a
+// counter should be zero.
+constexpr size_t kRouterCounterBytes =
+    ((size_t)(kRouterMaxT / kRouterTokensPerCta) * sizeof(unsigned) + 255) & ~(size_t)255;
 
 struct RouterParams {
   const __nv_bfloat16* x;     // [T, H]
@@ -163,8 +170,8 @@ extern "C" {
 
 size_t d3_router_workspace_size(int32_t T, int32_t E) {
   if (T <= 0 || E <= 0) return 0;
-  const size_t tiles = (size_t)(T + kRouterTokensPerCta - 1) / kRouterTokensPerCta;
-  return align256((size_t)T * E * sizeof(float)) + align256(tiles * sizeof(unsigned));
+  if (T > kRouterMaxT) return 0;
+  return kRouterCounterBytes + align256((size_t)T * E * sizeof(float));
 }
 
 int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int32_t E,
@@ -172,7 +179,7 @@ int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int3
                    void* weights_bf16_out, void* workspace, size_t workspace_bytes,
                    d3_stream_t stream) {
   D3_CHECK_ARG(x && gate_w && ids_out, "d3_router_topk: null pointer");
-  D3_CHECK_ARG(T >= 1, "T must be >= 1");
+  if (T < 1 || T > kRouterMaxT) return fail(D3_ERR_TOO_LARGE, "T must be in [1, %d]", kRouterMaxT);
   D3_CHECK_ARG(H >= 8 && H % 8 == 0 && H <= kRouterMaxH, "H must be a multiple of 8 in [8, %d]",
                kRouterMaxH);
   D3_CHECK_ARG(E >= 1 && E <= kRouterMaxE, "E must be in [1, %d]", kRouterMaxE);
@@ -189,9 +196,8 @@ int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int3
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.w = static_cast<const __nv_bfloat16*>(gate_w);
   p.T = T; p.H = H; p.E = E; p.topk = topk; p.renorm = renorm;
-  p.logits = static_cast<float*>(workspace);
-  p.arrivals = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) +
-                                           align256((size_t)T * E * sizeof(float)));
+  p.arrivals = static_cast<unsigned*>(workspace);
+  p.logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kRouterCounterBytes);
   p.ids_out = ids_out;
   p.weights_out = weights_out;
   p.weights_bf16_out = static_cast<__nv_bfloat16*>(weights_bf16_out);

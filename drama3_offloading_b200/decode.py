@@ -1,0 +1,155 @@
+"""40-layer Drama-3-shaped MoE decode stack with experts offloaded to pinned host
+memory -- the production configuration of the reference (device cache + fetch
+kernel + CUDA graphs, bin/narrate.py:573-650, notes/12-full-run.md:6-10),
+random-initialised at the real shapes.
+
+Per layer and decode token (batch 1):
+
+1. dense stand-in: ``h += down(silu(up(h)))`` with bf16 weights sized so the
+   40 layers read 6.9 GiB per token -- the non-expert (attention / GDN /
+   shared-expert / projection) weight traffic of Drama-3 (notes/01-static-
+   findings.md:54-55).  Plain cuBLAS GEMVs: not part of the hot path.
+2. router ``d3_router_topk`` on the layer's bf16 gate [256, 2048].
+3. ``d3_resolve_fetch``: device slot allocator + fetch of the missed experts
+   from pinned host memory into the layer's device cache.
+4. ``d3_moe_fp8_forward`` on the cache slots, then ``h = rms(h + moe)``.
+
+Routing: the router runs every layer (its cost is real), but the expert ids
+fed to the cache come from the seeded Zipf(1.1) trace so hit rates are those
+of skewed real routing rather than of a random-init gate (which routes almost
+uniformly).  The router's weights are used for the combine.
+
+The whole token step is captured into one CUDA graph; the trace position is a
+device counter, so replays walk the trace.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib, devcache, moe
+from .stack import OffloadedExperts
+
+DENSE_GIB = 6.9
+
+
+class DecodeStack:
+    def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048, inter: int = 512,
+                 topk: int = 8, cache_gib: float = 8.0, capacity: int | None = None,
+                 dense_gib: float = DENSE_GIB, trace: np.ndarray | None = None, device="cuda",
+                 policy: str = "lru", seed: int = 0, fill: str = "random"):
+        self.device = dev = torch.device(device)
+        self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
+        per_expert = 2 * inter * hidden + hidden * inter + 4 * (2 * inter * hidden + hidden * inter) // (128 * 128)
+        self.capacity = capacity or max(1, int(cache_gib * (1 << 30)) // (layers * per_expert))
+        self.store = OffloadedExperts(layers, experts, hidden, inter, self.capacity, dev, seed,
+                                      policy, fill)
+        g = torch.Generator(device=dev).manual_seed(seed + 7)
+        # dense stand-in: 2 * R * H bf16 per layer
+        per_layer = dense_gib * (1 << 30) / layers
+        R = max(128, int(per_layer / (2 * hidden * 2)) // 128 * 128)
+        self.R = R
+        self.up = [torch.randn(R, hidden, generator=g, device=dev, dtype=torch.bfloat16) * (hidden ** -0.5)
+                   for _ in range(layers)]
+        self.down = [torch.randn(hidden, R, generator=g, device=dev, dtype=torch.bfloat16) * (R ** -0.5 * 0.5)
+                     for _ in range(layers)]
+        self.dense_bytes = sum(t.numel() * 2 for t in self.up + self.down)
+        self.gate = [(torch.randn(experts, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                     for _ in range(layers)]
+        self.h = torch.zeros(1, hidden, dtype=torch.bfloat16, device=dev)
+        self.ids = torch.empty(1, topk, dtype=torch.int32, device=dev)
+        self.wts = torch.empty(1, topk, dtype=torch.float32, device=dev)
+        self.moe_out = torch.empty(1, hidden, dtype=torch.bfloat16, device=dev)
+        if trace is None:
+            from .trace import zipf_trace
+            trace = zipf_trace(steps=4096, layers=layers, experts=experts, k=topk)
+        self.trace_steps = trace.shape[0]
+        self.trace_dev = torch.from_numpy(trace.astype(np.int32)).to(dev)
+        self.step_idx = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.graph = None
+        # warm the library (workspaces, smem attributes) outside any capture
+        moe.router_topk(self.h, self.gate[0], topk, out_ids=self.ids, out_w=self.wts)
+
+    # ---------------------------------------------------------------- one token
+    def _layer(self, l: int, cur_ids: torch.Tensor) -> None:
+        h = self.h
+        a = torch.nn.functional.silu(h @ self.up[l].t())
+        h = h + a @ self.down[l].t()
+        moe.router_topk(h, self.gate[l], self.k, out_ids=self.ids, out_w=self.wts)
+        ex = self.store.layers[l]
+        slots = devcache.dev_resolve_and_fetch(ex, cur_ids[l])
+        moe.fp8_moe_forward(h, slots.reshape(1, self.k), self.wts, ex._dc_w13, ex._dc_s13,
+                            ex._dc_w2, ex._dc_s2, out=self.moe_out)
+        y = (h + self.moe_out).float()
+        y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6)
+        self.h.copy_(y.to(torch.bfloat16))
+
+    def step(self) -> None:
+        """One decode token through all layers (eager; capturable)."""
+        cur = self.trace_dev.index_select(0, self.step_idx)[0]
+        self.step_idx.add_(1).remainder_(self.trace_steps)
+        for l in range(self.L):
+            self._layer(l, cur)
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.step()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        self.graph = g
+        self.reset()
+        return g
+
+    def reset(self) -> None:
+        """Cold caches, trace at step 0, zero hidden state (addresses unchanged)."""
+        self.store.reset_caches()
+        self.step_idx.zero_()
+        self.h.zero_()
+        torch.cuda.synchronize(self.device)
+
+    def sample_fetch_timing(self, steps: int) -> dict:
+        """Eager decode steps with CUDA events around every layer's allocator +
+        fetch launch pair (same stream): bytes fetched and device time, for the
+        fetch kernel's achieved host-link bandwidth."""
+        evs = []
+        c0 = self.store.counters()
+        for _ in range(steps):
+            cur = self.trace_dev.index_select(0, self.step_idx)[0]
+            self.step_idx.add_(1).remainder_(self.trace_steps)
+            for l in range(self.L):
+                h = self.h
+                a = torch.nn.functional.silu(h @ self.up[l].t())
+                h = h + a @ self.down[l].t()
+                moe.router_topk(h, self.gate[l], self.k, out_ids=self.ids, out_w=self.wts)
+                ex = self.store.layers[l]
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                slots = devcache.dev_resolve_and_fetch(ex, cur[l])
+                e1.record()
+                evs.append((e0, e1))
+                moe.fp8_moe_forward(h, slots.reshape(1, self.k), self.wts, ex._dc_w13,
+                                    ex._dc_s13, ex._dc_w2, ex._dc_s2, out=self.moe_out)
+                y = (h + self.moe_out).float()
+                y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6)
+                self.h.copy_(y.to(torch.bfloat16))
+        torch.cuda.synchronize(self.device)
+        c1 = self.store.counters()
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+        return {"bytes": c1["bytes_fetched"] - c0["bytes_fetched"], "ms": ms,
+                "launch_pairs": len(evs), "misses": c1["misses"] - c0["misses"]}
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library launched per token (router, allocator, fetch,
+        route, quant, gemm1, act, gemm2, combine per layer)."""
+        return 9 * self.L
+
+    def roofline_ms(self, hits: float, misses: float, hbm_gbs: float, host_gbs: float) -> float:
+        """t >= dense/HBM + hits*expert/HBM + misses*expert/host per token."""
+        eb = devcache.EXPERT_BYTES
+        return 1e3 * (self.dense_bytes / (hbm_gbs * 1e9) + hits * eb / (hbm_gbs * 1e9)
+                      + misses * eb / (host_gbs * 1e9))

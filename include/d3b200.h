@@ -149,8 +149,8 @@ D3_API size_t d3_router_workspace_size(int32_t T, int32_t E);
  * renorm != 0.  Logits are the exactly rounded bf16 of each dot product.
  * Outputs: ids_out int32 [T,k]; weights_out f32 [T,k] and/or
  * weights_bf16_out bf16 [T,k] (either may be NULL).  The workspace must be
- * zero-filled once before its first use (every call leaves it reusable).
- * Limits: H % 8 == 0, H <= 8192, E <= 1024, k <= 32.
+ * zero-filled once before its first use (every call leaves it reusable, for
+ * any T).  Limits: T <= 65536, H % 8 == 0, H <= 8192, E <= 1024, k <= 32.
  * Replaces the upstream MoE block's gate -> softmax -> topk -> renorm
  * (fish-speech moe.py:217-220, quoted at notes/01-static-findings.md:133-138),
  * whose topk_ids feed dev_cached_forward -- bin/devcache.py:258-277. */
