@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "d3_fetch_jobs": (ctypes.c_int, [ctypes.POINTER(LayerCache), I32, P]),
     "d3_router_workspace_size": (SZ, [I32, I32]),
     "d3_router_topk": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, P, P, P, P, SZ, P]),
+    "d3_router_topk_noalloc": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, P, P, P, P]),
     "d3_moe_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "d3_moe_fp8_forward": (ctypes.c_int, [P, P, I32, P, I32, I32, I32, P, P, P, P, I32, I32,
                                           I32, P, P, P, SZ, P]),

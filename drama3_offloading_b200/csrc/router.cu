@@ -20,6 +20,8 @@
 
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 namespace d3 {
 
 constexpr int kRouterExpertsPerCta = 8;   // one per warp
@@ -210,6 +212,100 @@ int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int3
                 "router smem attribute");
   router_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(p);
   return launch_status("router_kernel launch");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ no-allocation router
+//
+// d3_router_topk_noalloc serves callers that cannot hand the router a device
+// workspace: a host runtime that binds only this C ABI and has no device
+// allocator of its own, a serving loop that must not take an allocator lock
+// or risk an out-of-memory error mid-decode, or a process that already gave
+// every free byte of device memory to the expert cache (the reference sizes
+// its cache to all free VRAM, bin/offload.py:611-661).  Its scratch -- the
+// per-token-tile arrival counters and the logits -- lives in the file-scope
+// array below, reserved once per GPU when the library's device code is loaded
+// and kept until the process exits.
+
+namespace d3 {
+
+constexpr int kNoAllocMaxT = 2048;                  // tokens per call
+constexpr size_t kNoAllocMaxLogits = 65536;         // T * E per call (256 KiB of fp32)
+constexpr size_t kNoAllocCounterBytes = 1024;       // 256 tiles of 8 tokens
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocMaxLogits * sizeof(float);
+
+static __device__ __align__(256) unsigned char g_router_scratch[kNoAllocScratchBytes];
+
+// Device address of g_router_scratch on the current device.  The name is only
+// a host-side stand-in in host code, so the address is looked up once per
+// device (with that device current) and cached.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  D3_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(D3_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_router_scratch)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return D3_OK;
+}
+
+}  // namespace d3
+
+extern "C" {
+
+int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t H, int32_t E,
+                           int32_t topk, int32_t renorm, int32_t* ids_out, float* weights_out,
+                           void* weights_bf16_out, d3_stream_t stream) {
+  D3_CHECK_ARG(x && gate_w && ids_out, "d3_router_topk_noalloc: null pointer");
+  if (T < 1 || T > kNoAllocMaxT)
+    return fail(D3_ERR_TOO_LARGE, "d3_router_topk_noalloc: T must be in [1, %d] (got %d)",
+                kNoAllocMaxT, T);
+  D3_CHECK_ARG(H >= 8 && H % 8 == 0 && H <= kRouterMaxH, "H must be a multiple of 8 in [8, %d]",
+               kRouterMaxH);
+  D3_CHECK_ARG(E >= 1 && E <= kRouterMaxE, "E must be in [1, %d]", kRouterMaxE);
+  if ((size_t)T * (size_t)E > kNoAllocMaxLogits)
+    return fail(D3_ERR_TOO_LARGE,
+                "d3_router_topk_noalloc: T*E = %zu exceeds the built-in scratch (%zu logits); "
+                "use d3_router_topk with a workspace",
+                (size_t)T * (size_t)E, kNoAllocMaxLogits);
+  D3_CHECK_ARG(topk >= 1 && topk <= 32 && topk <= E, "topk must be in [1, min(32, E)]");
+  if (!aligned16(x) || !aligned16(gate_w))
+    return fail(D3_ERR_MISALIGNED, "x and gate_w must be 16-byte aligned");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // The arrival counters must start at zero; clear the ones this call uses
+  // (a memset on the stream, no allocation).
+  const size_t tiles = (size_t)(T + kRouterTokensPerCta - 1) / kRouterTokensPerCta;
+  D3_CUDA_TRY(cudaMemsetAsync(scratch, 0, tiles * sizeof(unsigned), st),
+              "clear router scratch counters");
+  RouterParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.w = static_cast<const __nv_bfloat16*>(gate_w);
+  p.T = T; p.H = H; p.E = E; p.topk = topk; p.renorm = renorm;
+  p.arrivals = static_cast<unsigned*>(scratch);
+  p.logits = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
+  p.ids_out = ids_out;
+  p.weights_out = weights_out;
+  p.weights_bf16_out = static_cast<__nv_bfloat16*>(weights_bf16_out);
+  const dim3 grid((unsigned)((E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
+                  (unsigned)tiles);
+  const size_t smem = (size_t)kRouterTokensPerCta * H * sizeof(__nv_bfloat16);
+  if (smem > 48 * 1024)
+    D3_CUDA_TRY(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "router smem attribute");
+  router_kernel<<<grid, 256, smem, st>>>(p);
+  return launch_status("router_kernel launch (no-alloc)");
 }
 
 }  // extern "C"

@@ -159,6 +159,23 @@ D3_API int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t 
                           void* weights_bf16_out, void* workspace, size_t workspace_bytes,
                           d3_stream_t stream);
 
+/* d3_router_topk without a workspace argument, for callers that cannot
+ * allocate device memory (a runtime that binds only this C ABI and has no
+ * device allocator, a serving loop that must never allocate or risk an
+ * out-of-memory error mid-decode, a process whose free device memory all went
+ * to the expert cache).  No counterpart in the reference; it allocates
+ * nothing.  Same inputs, outputs and results as d3_router_topk.
+ * Scratch: a fixed array of 1 KiB + 256 KiB inside the library, reserved on
+ * every GPU that loads it until the process exits.  Limits: T <= 2048 and
+ * T * E <= 65536 (e.g. T = 256 at E = 256); larger calls return
+ * D3_ERR_TOO_LARGE.  The first call on each device looks the array's device
+ * address up, so make it before any stream capture on that device.  All
+ * calls share the one array, so calls that overlap on the GPU (different
+ * streams, or concurrent graphs) race: serialise them. */
+D3_API int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t H,
+                                  int32_t E, int32_t topk, int32_t renorm, int32_t* ids_out,
+                                  float* weights_out, void* weights_bf16_out, d3_stream_t stream);
+
 /* ------------------------------------------------------------- expert GEMM */
 
 /* Workspace bytes d3_moe_fp8_forward needs (0 = unsupported shape). */
