@@ -201,10 +201,12 @@ def run_decode(args, rank, world, local):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with benchutil.ClockSampler(local) as clk:
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("timed")
         a.record()
         for _ in range(args.steps):
             g.replay()
         b.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(dev)
     benchutil.barrier(world, dev)
     ms = a.elapsed_time(b)
@@ -289,10 +291,12 @@ def run_fetch(args, rank, world, local):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with benchutil.ClockSampler(local) as clk:
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("timed")
         a.record()
         for _ in range(args.steps):
             g.replay()
         b.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(dev)
     benchutil.barrier(world, dev)
     ms = a.elapsed_time(b)
