@@ -60,7 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "d3_router_topk_noalloc": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, P, P, P, P]),
     "d3_moe_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "d3_moe_fp8_forward": (ctypes.c_int, [P, P, I32, P, I32, I32, I32, P, P, P, P, I32, I32,
-                                          I32, P, P, P, SZ, P]),
+                                          I32, P, I32, P, P, SZ, P]),
 }
 
 _lib = None

@@ -40,6 +40,26 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int num_sms();          // SM count of the current device (cached per device)
 bool pdl_enabled();     // programmatic dependent launch on (env D3_NO_PDL unset)
 
+// Launch `kernel`, optionally as a programmatic dependent of the previous
+// launch on the stream: its CTAs may become resident while that grid drains,
+// and every kernel of this library calls griddepcontrol.wait before touching
+// global memory another launch produced or consumes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ---------------------------------------------------------------- device side
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

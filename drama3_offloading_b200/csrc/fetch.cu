@@ -184,41 +184,74 @@ __device__ __forceinline__ void warp_argmin(int64_t& key, int& idx) {
 
 // One warp.  LRU: the _resolve_slots decision sequence.  LFU: victim is the
 // lexicographic min of (used this step, uses since insert, insertion seq).
-// Dynamic shared memory: stamp[C] (+ freq[C], ins[C] for LFU), int64.
+// Every table read the decisions depend on is prefetched in parallel before
+// the sequential loop (the k ids, their slot_of entries, the C stamps and
+// slot owners into shared memory), so the loop itself touches only registers
+// and shared memory; lane 0 streams the table updates out to global memory.
+// A prefetched slot_of entry is still valid iff the slot's owner is still
+// that expert; an id seen earlier in the same call resolves to the slot its
+// latest occurrence got (again iff still owned) -- together exactly the
+// reference's live slot_of lookup.
+// Dynamic shared memory: stamp[C] (+ freq[C], ins[C] for LFU) int64, then
+// owner[C] int32.
 __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   extern __shared__ int64_t sh[];
-  int64_t* s_stamp = sh;
-  int64_t* s_freq = sh + p.capacity;
-  int64_t* s_ins = sh + 2 * p.capacity;
-  const int lane = threadIdx.x;
   const int C = p.capacity;
   const bool lfu = p.policy == D3_POLICY_LFU;
+  int64_t* s_stamp = sh;
+  int64_t* s_freq = sh + C;
+  int64_t* s_ins = sh + 2 * C;
+  int32_t* s_owner = reinterpret_cast<int32_t*>(sh + (lfu ? 3 : 1) * C);
+  const int lane = threadIdx.x;
+  const unsigned full = 0xffffffffu;
   pdl_trigger();  // the dependent fetch grid may start launching now
+  pdl_wait();     // ids may come from the launch just before this one
+  // ---- parallel prefetch
+  int e_lo = -1, e_hi = -1, pre_lo = -1, pre_hi = -1;
+  if (lane < p.k) {
+    e_lo = load_id(p.ids, p.ids_bytes, lane);
+    if (e_lo >= p.num_experts) e_lo = -1;
+    if (e_lo >= 0) pre_lo = p.slot_of[e_lo];
+  }
+  if (lane + 32 < p.k) {
+    e_hi = load_id(p.ids, p.ids_bytes, lane + 32);
+    if (e_hi >= p.num_experts) e_hi = -1;
+    if (e_hi >= 0) pre_hi = p.slot_of[e_hi];
+  }
   for (int c = lane; c < C; c += 32) {
     s_stamp[c] = p.stamp[c];
+    s_owner[c] = p.slot_expert[c];
     if (lfu) { s_freq[c] = p.freq[c]; s_ins[c] = p.ins[c]; }
   }
   const int64_t step = *p.step + 1;
   __syncwarp();
+  int out_lo = -1, out_hi = -1;
   int nmiss = 0, hits = 0;
   for (int i = 0; i < p.k; ++i) {
-    const int32_t e = load_id(p.ids, p.ids_bytes, i);
-    if (e < 0 || e >= p.num_experts) {
+    const int src = i & 31;
+    const int32_t e = __shfl_sync(full, i < 32 ? e_lo : e_hi, src);
+    int32_t s = __shfl_sync(full, i < 32 ? pre_lo : pre_hi, src);
+    if (e < 0) {
       if (lane == 0) p.out_slot[i] = -1;
-      continue;
+      continue;  // out_lo/out_hi stay -1 for this i
     }
-    int32_t s = lane == 0 ? p.slot_of[e] : 0;  // lane 0 owns all table reads/writes
-    s = __shfl_sync(0xffffffffu, s, 0);
+    if (s >= 0 && s_owner[s] != e) s = -1;  // evicted earlier in this call
     if (s < 0) {
-      int64_t key;
+      // latest earlier occurrence of e in this call
+      const unsigned m_lo = __ballot_sync(full, lane < i && e_lo == e);
+      const unsigned m_hi = __ballot_sync(full, lane + 32 < i && e_hi == e);
+      const int j = m_hi ? 32 + (31 - __clz(m_hi)) : (m_lo ? 31 - __clz(m_lo) : -1);
+      const int sj = __shfl_sync(full, j >= 32 ? out_hi : out_lo, j >= 0 ? (j & 31) : 0);
+      if (j >= 0 && sj >= 0 && s_owner[sj] == e) s = sj;
+    }
+    if (s < 0) {
       int best = 0x7fffffff;
       if (!lfu) {
-        key = INT64_MAX;
+        int64_t key = INT64_MAX;
         for (int c = lane; c < C; c += 32)
           if (s_stamp[c] < key) { key = s_stamp[c]; best = c; }
         warp_argmin(key, best);
       } else {
-        // three-part key, reduced lexicographically
         int64_t bu = INT64_MAX, bf = INT64_MAX, bi = INT64_MAX;
         for (int c = lane; c < C; c += 32) {
           const int64_t u = s_stamp[c] == step ? 1 : 0, f = s_freq[c], n = s_ins[c];
@@ -228,20 +261,21 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
-          const int64_t ou = __shfl_xor_sync(0xffffffffu, bu, off);
-          const int64_t of = __shfl_xor_sync(0xffffffffu, bf, off);
-          const int64_t on = __shfl_xor_sync(0xffffffffu, bi, off);
-          const int oc = __shfl_xor_sync(0xffffffffu, best, off);
+          const int64_t ou = __shfl_xor_sync(full, bu, off);
+          const int64_t of = __shfl_xor_sync(full, bf, off);
+          const int64_t on = __shfl_xor_sync(full, bi, off);
+          const int oc = __shfl_xor_sync(full, best, off);
           if (ou < bu || (ou == bu && (of < bf || (of == bf && (on < bi || (on == bi && oc < best)))))) {
             bu = ou; bf = of; bi = on; best = oc;
           }
         }
       }
       if (lane == 0) {
-        const int32_t victim = p.slot_expert[best];
+        const int32_t victim = s_owner[best];
         if (victim >= 0) p.slot_of[victim] = -1;
         p.slot_of[e] = best;
         p.slot_expert[best] = e;
+        s_owner[best] = e;
         p.fetch_slot[nmiss] = best;
         p.fetch_expert[nmiss] = e;
         if (lfu) {
@@ -264,7 +298,8 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
       }
       p.out_slot[i] = s;
     }
-    __syncwarp();  // lane 0's shared-memory stamp update is seen by the next scan
+    if (i < 32) { if (lane == i) out_lo = s; } else { if (lane == i - 32) out_hi = s; }
+    __syncwarp();  // lane 0's shared-memory updates are seen by the next id
   }
   if (lane == 0) {
     *p.step = step;
@@ -290,7 +325,8 @@ __global__ void lookup_kernel(const int32_t* __restrict__ slot_of, int32_t E, co
 // ---------------------------------------------------------------- host side
 
 static int launch_resolve(const ResolveParams& p, cudaStream_t st) {
-  const size_t smem = (size_t)p.capacity * sizeof(int64_t) * (p.policy == D3_POLICY_LFU ? 3 : 1);
+  const size_t smem = (size_t)p.capacity * sizeof(int64_t) * (p.policy == D3_POLICY_LFU ? 3 : 1) +
+                      (size_t)p.capacity * sizeof(int32_t);
   if (smem > 48 * 1024) {
     D3_CUDA_TRY(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),

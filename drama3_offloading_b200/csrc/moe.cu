@@ -147,7 +147,14 @@ struct RouteParams {
   int BN;
   int mt1, nkb1, kbps1, split1;
   int mt2, nkb2, kbps2, split2;
+  // activation quantisation folded into this launch for small batches
+  int fuse_quant;
+  const __nv_bfloat16* x; int topk, H, Ppad;
+  uint8_t* xq; float* xs;
 };
+
+__device__ void quant_x_block(const __nv_bfloat16* __restrict__ x, int pair, int topk, int H,
+                              int row, int kb, uint8_t* __restrict__ xq, float* __restrict__ xs);
 
 __device__ __forceinline__ int load_pair_id(const void* ids, int bytes, int i, int n) {
   long long v = bytes == 8 ? static_cast<const long long*>(ids)[i]
@@ -166,6 +173,8 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   int* tcount = sm + p.n;      // [n] N tiles per expert, then its prefix
   __shared__ int warp_tot[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();
   for (int e = tid; e < p.n; e += blockDim.x) cursor[e] = 0;
   __syncthreads();
   for (int i = tid; i < p.P; i += blockDim.x) {
@@ -239,7 +248,16 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
       __syncwarp();
     }
   }
+  // sorted positions past the valid pairs (skipped ids) hold -1
+  for (int i = warp_tot[31] + tid; i < p.P; i += blockDim.x) p.sorted[i] = -1;
   __syncthreads();
+  if (p.fuse_quant) {
+    const int nkb = p.H / 128;
+    for (int w = warp; w < p.Ppad * nkb; w += 32) {
+      const int row = w / nkb, kb = w - row * nkb;
+      quant_x_block(p.x, row < p.P ? p.sorted[row] : -1, p.topk, p.H, row, kb, p.xq, p.xs);
+    }
+  }
   // tile lists: for expert e, N tile j, split s, M tile m
   const int per_nt1 = p.mt1 * p.split1, per_nt2 = p.mt2 * p.split2;
   for (int e = lo; e < hi; ++e) {
@@ -290,16 +308,12 @@ __device__ __forceinline__ float quant_block(const float (&v)[4], uint32_t& hi4,
   return amax > 0.f ? amax / 448.f : 0.f;
 }
 
-// One warp per (sorted row, K block): x row of the pair's token -> planes.
-// Rows past the valid pairs (and up to Ppad) become zeros.
-__global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted,
-                               int P, int Ppad, int topk, int H, uint8_t* __restrict__ xq,
-                               float* __restrict__ xs) {
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+// One warp: the 128-wide K block kb of sorted row `row` (pair `pair`, or
+// zeros when pair < 0) -> hi/lo planes and scale.
+__device__ void quant_x_block(const __nv_bfloat16* __restrict__ x, int pair, int topk, int H,
+                              int row, int kb, uint8_t* __restrict__ xq, float* __restrict__ xs) {
+  const int lane = threadIdx.x & 31;
   const int nkb = H / 128;
-  if (gw >= Ppad * nkb) return;
-  const int row = gw / nkb, kb = gw - row * nkb;
-  const int pair = row < P ? sorted[row] : -1;
   float v[4];
   uint8_t* qrow = xq + (size_t)row * 2 * H;
   if (pair < 0) {  // rows past the valid pairs (skipped ids)
@@ -319,11 +333,27 @@ __global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* _
   if (lane == 0) xs[(size_t)row * nkb + kb] = s;
 }
 
+// One warp per (sorted row, K block): x row of the pair's token -> planes.
+// Rows past the valid pairs (and up to Ppad) become zeros.
+__global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted,
+                               int P, int Ppad, int topk, int H, uint8_t* __restrict__ xq,
+                               float* __restrict__ xs) {
+  pdl_trigger();
+  pdl_wait();
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nkb = H / 128;
+  if (gw >= Ppad * nkb) return;
+  const int row = gw / nkb, kb = gw - row * nkb;
+  quant_x_block(x, row < P ? sorted[row] : -1, topk, H, row, kb, xq, xs);
+}
+
 // One warp per (sorted row, K block of I): sum splits, SwiGLU, quantise.
 // Rows at or past the valid pair count (device word) become zeros.
 __global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int Ppad,
                            const int* __restrict__ nvalid_ptr, int I, uint8_t* __restrict__ hq,
                            float* __restrict__ hs) {
+  pdl_trigger();
+  pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int nkb = I / 128;
   if (gw >= Ppad * nkb) return;
@@ -348,14 +378,23 @@ __global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int 
   if (lane == 0) hs[(size_t)row * nkb + kb] = s;
 }
 
-// out[t, j] = bf16( sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
+// out[t, j] = bf16( [out[t,j] +] sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
 __global__ void combine_kernel(const float* __restrict__ ws2, int split, int P, int H,
                                const int* __restrict__ inv, const void* __restrict__ weights,
-                               int weights_f32, int T, int topk, __nv_bfloat16* __restrict__ out) {
+                               int weights_f32, int T, int topk, int accumulate,
+                               __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || j >= H) return;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (accumulate) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(out + (size_t)t * H + j);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[q] = __bfloat162float(b[q]);
+  }
   for (int k = 0; k < topk; ++k) {
     const int pos = inv[t * topk + k];
     if (pos < 0) continue;
@@ -447,6 +486,10 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // everything above is CTA-local set-up that overlaps the previous launch;
+  // the tile list and operands are produced upstream
+  pdl_trigger();
+  pdl_wait();
   const int ntiles = *p.ntiles;
 
   if (warp == 0) {
@@ -584,8 +627,10 @@ static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmP
   int grid = num_sms();
   if (max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  moe_gemm_kernel<BN><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(tw, tx, gp);
-  return launch_status("moe_gemm_kernel launch");
+  D3_CUDA_TRY(launch_k(moe_gemm_kernel<BN>, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st,
+                       pdl_enabled(), tw, tx, gp),
+              "moe_gemm_kernel launch");
+  return D3_OK;
 }
 
 }  // namespace d3
@@ -605,8 +650,8 @@ size_t d3_moe_workspace_size(int32_t T, int32_t topk, int32_t n_experts, int32_t
 int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const void* weights,
                        int32_t weights_f32, int32_t T, int32_t topk, const void* w13,
                        const float* s13, const void* w2, const float* s2, int32_t n_experts,
-                       int32_t H, int32_t I, void* out, int32_t* err_word, void* workspace,
-                       size_t workspace_bytes, d3_stream_t stream) {
+                       int32_t H, int32_t I, void* out, int32_t accumulate, int32_t* err_word,
+                       void* workspace, size_t workspace_bytes, d3_stream_t stream) {
   D3_CHECK_ARG(x && ids && weights && w13 && s13 && w2 && s2 && out && err_word,
                "d3_moe_fp8_forward: null pointer");
   D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
@@ -638,24 +683,27 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   rp.BN = pl.BN;
   rp.mt1 = 2 * I / 128; rp.nkb1 = H / 128; rp.kbps1 = pl.kbps1; rp.split1 = pl.split1;
   rp.mt2 = H / 128; rp.nkb2 = I / 128; rp.kbps2 = pl.kbps2; rp.split2 = pl.split2;
+  uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
+  float* xs = (float*)(ws + pl.o_xs);
+  // small batches quantise inside the route launch (one CTA, 32 warps)
+  rp.fuse_quant = (long)pl.Ppad * (H / 128) <= 32L * 32 ? 1 : 0;
+  rp.x = static_cast<const __nv_bfloat16*>(x);
+  rp.topk = topk; rp.H = H; rp.Ppad = pl.Ppad; rp.xq = xq; rp.xs = xs;
+  const bool pdl = pdl_enabled();
   const size_t rsmem = sizeof(int) * 2 * (size_t)n_experts;
   if (rsmem > 48 * 1024)
     D3_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)rsmem),
                 "route smem attribute");
-  // rows of `sorted` past the valid pairs stay -1 so quant writes zeros there
-  D3_CUDA_TRY(cudaMemsetAsync(rp.sorted, 0xFF, sizeof(int) * (size_t)P, st), "memset sorted");
-  route_kernel<<<1, 1024, rsmem, st>>>(rp);
-  int rc = launch_status("route_kernel launch");
-  if (rc) return rc;
-
-  uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
-  float* xs = (float*)(ws + pl.o_xs);
-  {
+  D3_CUDA_TRY(launch_k(route_kernel, dim3(1), dim3(1024), rsmem, st, pdl, rp),
+              "route_kernel launch");
+  int rc = D3_OK;
+  if (!rp.fuse_quant) {
     const long warps = (long)pl.Ppad * (H / 128);
-    quant_x_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), rp.sorted, P, pl.Ppad, topk, H, xq, xs);
-    if ((rc = launch_status("quant_x_kernel launch"))) return rc;
+    D3_CUDA_TRY(launch_k(quant_x_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+                         st, pdl, static_cast<const __nv_bfloat16*>(x), (const int*)rp.sorted, P,
+                         pl.Ppad, topk, H, xq, xs),
+                "quant_x_kernel launch");
   }
   CUtensorMap tw1, tx1, tw2, tx2;
   if ((rc = make_tmap_u8(&tw1, w13, H, (uint64_t)n_experts * 2 * I, H, 128))) return rc;
@@ -674,9 +722,10 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   float* hs = (float*)(ws + pl.o_hs);
   {
     const long warps = (long)pl.Ppad * (I / 128);
-    act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
-        ws1, pl.split1, P, pl.Ppad, rp.ntiles + 2, I, hq, hs);
-    if ((rc = launch_status("act_kernel launch"))) return rc;
+    D3_CUDA_TRY(launch_k(act_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st,
+                         pdl, (const float*)ws1, pl.split1, P, pl.Ppad,
+                         (const int*)(rp.ntiles + 2), I, hq, hs),
+                "act_kernel launch");
   }
   if ((rc = make_tmap_u8(&tw2, w2, I, (uint64_t)n_experts * H, I, 128))) return rc;
   if ((rc = make_tmap_u8(&tx2, hq, 2 * I, pl.Ppad, 2 * I, pl.BN))) return rc;
@@ -691,9 +740,10 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   if (rc) return rc;
   {
     const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
-    combine_kernel<<<grid, 128, 0, st>>>(ws2, pl.split2, P, H, rp.inv, weights, weights_f32, T,
-                                         topk, static_cast<__nv_bfloat16*>(out));
-    if ((rc = launch_status("combine_kernel launch"))) return rc;
+    D3_CUDA_TRY(launch_k(combine_kernel, grid, dim3(128), 0, st, pdl, (const float*)ws2,
+                         pl.split2, P, H, (const int*)rp.inv, weights, weights_f32, T, topk,
+                         accumulate ? 1 : 0, static_cast<__nv_bfloat16*>(out)),
+                "combine_kernel launch");
   }
   return D3_OK;
 }

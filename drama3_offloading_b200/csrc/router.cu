@@ -72,19 +72,33 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
 #pragma unroll
     for (int t = 0; t < kRouterTokensPerCta; ++t) acc[t] = 0.0;
     const uint4* wrow = reinterpret_cast<const uint4*>(p.w + (size_t)e * p.H);
-    for (int c = lane; c < vec_per_row; c += 32) {
-      const uint4 wv = __ldg(wrow + c);
-      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
-      double wd[8];
+    // issue all of a lane's gate-row loads (8 x 16 B for H = 2048) before any
+    // arithmetic, so the row streams in one memory latency
+    constexpr int kU = 8;
+    for (int c0 = lane; c0 < vec_per_row; c0 += 32 * kU) {
+      uint4 wv[kU];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) wd[q] = (double)__bfloat162float(wb[q]);
+      for (int u = 0; u < kU; ++u) {
+        const int c = c0 + 32 * u;
+        wv[u] = c < vec_per_row ? __ldg(wrow + c) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int t = 0; t < kRouterTokensPerCta; ++t) {
-        if (t < nt) {
-          const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
-          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+      for (int u = 0; u < kU; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= vec_per_row) break;
+        const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
+        double wd[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc[t] = fma((double)__bfloat162float(xb[q]), wd[q], acc[t]);
+        for (int q = 0; q < 8; ++q) wd[q] = (double)__bfloat162float(wb[q]);
+#pragma unroll
+        for (int t = 0; t < kRouterTokensPerCta; ++t) {
+          if (t < nt) {
+            const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              acc[t] = fma((double)__bfloat162float(xb[q]), wd[q], acc[t]);
+          }
         }
       }
     }

@@ -79,10 +79,13 @@ def workspace_bytes(T: int, topk: int, n_experts: int, H: int, I: int) -> int:
 
 def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                     w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
-                    out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, accumulate: bool = False,
+                    stream=None) -> torch.Tensor:
     """Routed MoE over block-scaled FP8 experts; returns bf16 [T, H].
 
-    ids (int32/int64) out of range -- e.g. -1 -- contribute nothing."""
+    ids (int32/int64) out of range -- e.g. -1 -- contribute nothing.  With
+    ``accumulate=True`` the result is added to ``out`` (which may be ``x``
+    itself: the block's residual add)."""
     if x.dtype != torch.bfloat16:
         raise TypeError("x must be bf16")
     x = x.contiguous()
@@ -109,7 +112,11 @@ def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
         raise TypeError("scales must be float32")
     dev = x.device
     if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs an out tensor")
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    elif out.dtype != torch.bfloat16 or not out.is_contiguous() or tuple(out.shape) != (T, H):
+        raise ValueError("out must be a contiguous bf16 [T, H] tensor")
     need = workspace_bytes(T, topk, n, H, I)
     if need == 0:
         raise ValueError(f"unsupported MoE shape T={T} topk={topk} n={n} H={H} I={I}")
@@ -117,5 +124,6 @@ def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     _lib.call("d3_moe_fp8_forward", _lib.ptr(x), _lib.ptr(ids), ids.element_size(),
               _lib.ptr(weights), 1 if weights.dtype == torch.float32 else 0, T, topk,
               _lib.ptr(w13), _lib.ptr(s13), _lib.ptr(w2), _lib.ptr(s2), n, H, I, _lib.ptr(out),
-              _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(), _lib.stream_ptr(stream))
+              1 if accumulate else 0, _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(),
+              _lib.stream_ptr(stream))
     return out

@@ -189,8 +189,10 @@ D3_API size_t d3_moe_workspace_size(int32_t T, int32_t topk, int32_t n_experts, 
  * skipped); weights f32 (weights_f32 = 1) or bf16 [T,topk]; w13 e4m3 [n,2I,H]
  * (gate rows [0,I), up rows [I,2I)), s13 f32 [n,2I/128,H/128]; w2 e4m3 [n,H,I],
  * s2 f32 [n,H/128,I/128] (weight = byte x scale of its 128x128 block);
- * out bf16 [T,H].  err_word: device int32, set non-zero (never cleared) if a
- * kernel gave up on a bounded wait.  Limits: H, I multiples of 128 in
+ * out bf16 [T,H], overwritten, or with accumulate != 0 added to (out may then
+ * alias x: the residual add of the MoE block).  err_word: device int32, set
+ * non-zero (never cleared) if a kernel gave up on a bounded wait.
+ * Limits: H, I multiples of 128 in
  * [128, 16384]; T*topk <= 65536; n_experts <= 8192.
  * Replaces upstream fp8_moe_forward(x, ids, w, w13, s13, w2, s2) as called by
  * dev_cached_forward -- bin/devcache.py:275-277 -- and the gather paths --
@@ -199,8 +201,8 @@ D3_API int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes,
                               const void* weights, int32_t weights_f32, int32_t T, int32_t topk,
                               const void* w13, const float* s13, const void* w2, const float* s2,
                               int32_t n_experts, int32_t H, int32_t I, void* out,
-                              int32_t* err_word, void* workspace, size_t workspace_bytes,
-                              d3_stream_t stream);
+                              int32_t accumulate, int32_t* err_word, void* workspace,
+                              size_t workspace_bytes, d3_stream_t stream);
 
 #ifdef __cplusplus
 }

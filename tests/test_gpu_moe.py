@@ -188,3 +188,17 @@ def test_dev_cached_forward_equals_resident(cap):
         got = devcache.dev_cached_forward(host, x, ids, w)
         assert torch.equal(want, got), f"cap {cap} step {step}"
     moe.check_errors(DEV)
+
+
+def test_moe_forward_accumulate_into_input():
+    """accumulate=True with out aliasing x: h <- h + moe(h) (the residual add)."""
+    ex, x, ids, w = _rand_case(16, 3, 8, 41)
+    xd = x.to(DEV)
+    plain = moe.fp8_moe_forward(xd, ids.to(DEV), w.to(DEV), ex.w13_weight, ex.w13_scale_inv,
+                                ex.w2_weight, ex.w2_scale_inv).clone()
+    h = xd.clone()
+    moe.fp8_moe_forward(h, ids.to(DEV), w.to(DEV), ex.w13_weight, ex.w13_scale_inv,
+                        ex.w2_weight, ex.w2_scale_inv, out=h, accumulate=True)
+    moe.check_errors(DEV)
+    want = xd.float() + plain.float()
+    assert rel_err(h, want) < 1e-2
