@@ -70,6 +70,14 @@ def init_dist(args):
     return rank, world, local
 
 
+def local_group(world):
+    """Process group of this machine's ranks (single-node runs: all ranks)."""
+    if world <= 1:
+        return None
+    import torch.distributed as dist
+    return dist.group.WORLD
+
+
 # ---------------------------------------------------------------- CPU legs (oracle)
 
 class CpuDecodeSample:
@@ -188,8 +196,11 @@ def run_decode(args, rank, world, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peak = benchutil.host_link_peak_gbs(device=dev)
+    # one shared host store per machine; each replica walks the trace from
+    # its own offset (independent token streams)
     stack = DecodeStack(layers=args.layers, cache_gib=args.cache_gib, device=dev,
-                        policy=args.policy)
+                        policy=args.policy, group=local_group(world), local_rank=local,
+                        trace_offset=512 * rank)
     from drama3_offloading_b200 import devcache
     devcache.FETCH_CTAS = args.fetch_ctas
     g = stack.capture()
@@ -261,7 +272,8 @@ def run_fetch(args, rank, world, local):
     trace = zipf_trace(steps=steps_total, layers=args.layers)
     peak = benchutil.host_link_peak_gbs(device=dev)
     store = OffloadedExperts(layers=args.layers, capacity=capacity, device=dev,
-                             policy=args.policy, fill="random")
+                             policy=args.policy, fill="random", group=local_group(world),
+                             local_rank=local)
     devcache.FETCH_CTAS = args.fetch_ctas
     trace_dev = torch.from_numpy(trace.astype(np.int32)).to(dev)
     step_idx = torch.zeros(1, dtype=torch.int64, device=dev)

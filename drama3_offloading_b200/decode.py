@@ -37,13 +37,15 @@ class DecodeStack:
     def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048, inter: int = 512,
                  topk: int = 8, cache_gib: float = 8.0, capacity: int | None = None,
                  dense_gib: float = DENSE_GIB, trace: np.ndarray | None = None, device="cuda",
-                 policy: str = "lru", seed: int = 0, fill: str = "random"):
+                 policy: str = "lru", seed: int = 0, fill: str = "random", group=None,
+                 local_rank: int = 0, trace_offset: int = 0):
         self.device = dev = torch.device(device)
         self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
         per_expert = 2 * inter * hidden + hidden * inter + 4 * (2 * inter * hidden + hidden * inter) // (128 * 128)
         self.capacity = capacity or max(1, int(cache_gib * (1 << 30)) // (layers * per_expert))
         self.store = OffloadedExperts(layers, experts, hidden, inter, self.capacity, dev, seed,
-                                      policy, fill)
+                                      policy, fill, group=group, local_rank=local_rank)
+        self.trace_offset = trace_offset
         g = torch.Generator(device=dev).manual_seed(seed + 7)
         # dense stand-in: 2 * R * H bf16 per layer
         per_layer = dense_gib * (1 << 30) / layers
@@ -65,7 +67,8 @@ class DecodeStack:
             trace = zipf_trace(steps=4096, layers=layers, experts=experts, k=topk)
         self.trace_steps = trace.shape[0]
         self.trace_dev = torch.from_numpy(trace.astype(np.int32)).to(dev)
-        self.step_idx = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.step_idx = torch.full((1,), trace_offset % self.trace_steps, dtype=torch.int64,
+                                   device=dev)
         self.graph = None
         # warm the library (workspaces, smem attributes) outside any capture
         moe.router_topk(self.h, self.gate[0], topk, out_ids=self.ids, out_w=self.wts)
@@ -109,9 +112,9 @@ class DecodeStack:
         return g
 
     def reset(self) -> None:
-        """Cold caches, trace at step 0, zero hidden state (addresses unchanged)."""
+        """Cold caches, trace at its start, zero hidden state (addresses unchanged)."""
         self.store.reset_caches()
-        self.step_idx.zero_()
+        self.step_idx.fill_(self.trace_offset % self.trace_steps)
         self.h.zero_()
         torch.cuda.synchronize(self.device)
 

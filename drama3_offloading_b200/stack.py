@@ -1,13 +1,13 @@
-"""A 40-layer Drama-3-shaped expert store in pinned host memory with per-layer
-device caches -- the offloaded configuration the reference runs in production
-(bin/offload.py:111-134 materialize_offloaded, :664-699 pin_experts;
-bin/devcache.py:280-301 install_dev_cache).
+"""A 40-layer Drama-3-shaped expert store in page-locked host memory with
+per-layer device caches -- the offloaded configuration the reference runs in
+production (bin/offload.py:111-134 materialize_offloaded, :664-699
+pin_experts; bin/devcache.py:280-301 install_dev_cache).
 
 Weights are random-init (no checkpoint): N(0, 0.02) quantised per 128x128
-block, generated on the GPU a few experts at a time and copied into
-page-locked host buffers (one pinned allocation per layer and buffer, as
-pin_experts does; every size is a power of two at the real dims, so the
-caching host allocator wastes nothing).
+block, generated on the GPU a few experts at a time and copied into the host
+store.  The store is one shared, page-locked allocation per machine
+(``hoststore.SharedHostStore``): local rank 0 fills it, every local rank maps
+it and keeps its own device cache.
 """
 from __future__ import annotations
 
@@ -16,18 +16,16 @@ import time
 import torch
 
 from . import devcache, synth
+from .hoststore import SharedHostStore, layer_bytes
 
 GiB = 1 << 30
 
 
-def pinned_layer(E: int, H: int, I: int, seed: int, device, fill: str = "random",
-                 gen_chunk: int = 32) -> synth.HostExperts:
-    host = synth.HostExperts(
-        E,
-        torch.empty(E, 2 * I, H, dtype=torch.float8_e4m3fn, pin_memory=True),
-        torch.empty(E, H, I, dtype=torch.float8_e4m3fn, pin_memory=True),
-        torch.empty(E, 2 * I // 128, H // 128, dtype=torch.float32, pin_memory=True),
-        torch.empty(E, H // 128, I // 128, dtype=torch.float32, pin_memory=True))
+def fill_layer(host: synth.HostExperts, seed: int, device, fill: str = "random",
+               gen_chunk: int = 32) -> None:
+    E = host.num_experts
+    H = host.w13_weight.shape[2]
+    I = host.w2_weight.shape[2]
     if fill == "random":
         for lo in range(0, E, gen_chunk):
             hi = min(E, lo + gen_chunk)
@@ -38,27 +36,44 @@ def pinned_layer(E: int, H: int, I: int, seed: int, device, fill: str = "random"
             host.w13_scale_inv[lo:hi].copy_(part.w13_scale_inv)
             host.w2_scale_inv[lo:hi].copy_(part.w2_scale_inv)
     elif fill == "zeros":
-        for n in ("w13_weight", "w2_weight"):
-            getattr(host, n).view(torch.uint8).zero_()
+        host.w13_weight.view(torch.uint8).zero_()
+        host.w2_weight.view(torch.uint8).zero_()
         host.w13_scale_inv.fill_(1.0)
         host.w2_scale_inv.fill_(1.0)
     else:
         raise ValueError(fill)
-    return host
 
 
 class OffloadedExperts:
-    """``layers`` pinned host expert stores, each with its own device cache."""
+    """``layers`` host expert stores (one shared page-locked allocation), each
+    with its own device cache on ``device``.
+
+    ``group``/``local_rank``: the ranks of this machine share one store; local
+    rank 0 fills it."""
 
     def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048,
                  inter: int = 512, capacity: int = 51, device="cuda", seed: int = 0,
-                 policy: str = "lru", fill: str = "random"):
+                 policy: str = "lru", fill: str = "random", group=None, local_rank: int = 0):
+        import torch.distributed as dist
         self.device = torch.device(device)
         self.H, self.I, self.E = hidden, inter, experts
         t0 = time.perf_counter()
-        self.layers = [pinned_layer(experts, hidden, inter, seed + l, self.device, fill)
-                       for l in range(layers)]
+        self.host = SharedHostStore(layers * layer_bytes(experts, hidden, inter), local_rank,
+                                    group)
+        self.layers = []
+        for l in range(layers):
+            ex = synth.HostExperts(
+                experts,
+                self.host.take((experts, 2 * inter, hidden), torch.float8_e4m3fn),
+                self.host.take((experts, hidden, inter), torch.float8_e4m3fn),
+                self.host.take((experts, 2 * inter // 128, hidden // 128), torch.float32),
+                self.host.take((experts, hidden // 128, inter // 128), torch.float32))
+            if self.host.owner:
+                fill_layer(ex, seed + l, self.device, fill)
+            self.layers.append(ex)
         torch.cuda.synchronize(self.device)
+        if group is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
+            dist.barrier(group=group, device_ids=[self.device.index])
         self.setup_s = time.perf_counter() - t0
         for ex in self.layers:
             devcache.init_dev_cache(ex, self.device, capacity, policy=policy)
