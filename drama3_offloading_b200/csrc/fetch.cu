@@ -416,14 +416,21 @@ int d3_device_ptr_of(const void* host, size_t bytes, void** dev_out) {
   void* dptr = nullptr;
   D3_CUDA_TRY(cudaHostGetDevicePointer(&dptr, const_cast<void*>(host), 0),
               "cudaHostGetDevicePointer");
-  // the whole range must lie in one mapped allocation
+  // the whole range must be page-locked and device-mapped contiguously (it
+  // may span adjacent registrations, whose device addresses then continue)
   if (bytes > 1) {
     cudaPointerAttributes last;
     const char* end = static_cast<const char*>(host) + bytes - 1;
     e = cudaPointerGetAttributes(&last, end);
-    if (e != cudaSuccess || last.type != cudaMemoryTypeHost) {
+    void* dend = nullptr;
+    if (e == cudaSuccess && last.type == cudaMemoryTypeHost)
+      e = cudaHostGetDevicePointer(&dend, const_cast<char*>(end), 0);
+    if (e != cudaSuccess || last.type != cudaMemoryTypeHost ||
+        static_cast<char*>(dend) != static_cast<char*>(dptr) + bytes - 1) {
       cudaGetLastError();
-      return fail(D3_ERR_NOT_PINNED, "range [%p, +%zu) leaves the pinned allocation", host, bytes);
+      return fail(D3_ERR_NOT_PINNED,
+                  "range [%p, +%zu) is not one contiguously mapped page-locked range", host,
+                  bytes);
     }
   }
   *dev_out = dptr;

@@ -22,6 +22,7 @@ import torch
 
 GiB = 1 << 30
 _REGISTER_PORTABLE_MAPPED = 1 | 2   # cudaHostRegisterPortable | cudaHostRegisterMapped
+_CHUNK = 1 << 30
 
 
 def mem_available() -> int:
@@ -77,13 +78,24 @@ class SharedHostStore:
             self.fd = os.open(f"/proc/{pid}/fd/{fd}", os.O_RDWR)
         self.mm = mmap.mmap(self.fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
         self.buf = torch.frombuffer(self.mm, dtype=torch.uint8)
-        self.registered = False
+        # Page-lock in 1 GiB pieces: several processes registering one large
+        # range of not-yet-faulted shared pages at the same time was refused
+        # by the OS (cudaErrorOperatingSystem) on this pool, piecewise
+        # registration of the same bytes was not.  Under unified addressing
+        # the pieces map at their host addresses, so a tensor may span two.
+        self.chunks = []
         if register:
             rt = torch.cuda.cudart()
-            rc = rt.cudaHostRegister(self.buf.data_ptr(), nbytes, _REGISTER_PORTABLE_MAPPED)
-            if int(rc) != 0:
-                raise RuntimeError(f"cudaHostRegister of the shared expert store failed ({rc})")
-            self.registered = True
+            base = self.buf.data_ptr()
+            for off in range(0, nbytes, _CHUNK):
+                n = min(_CHUNK, nbytes - off)
+                rc = int(rt.cudaHostRegister(base + off, n, _REGISTER_PORTABLE_MAPPED))
+                if rc != 0:
+                    self.close()
+                    raise RuntimeError(f"cudaHostRegister of the shared expert store failed "
+                                       f"(cudaError {rc}) at offset {off}")
+                self.chunks.append(base + off)
+        self.registered = bool(self.chunks)
         self._off = 0
 
     def take(self, shape, dtype) -> torch.Tensor:
@@ -99,9 +111,11 @@ class SharedHostStore:
         return t
 
     def close(self) -> None:
-        if getattr(self, "registered", False):
-            torch.cuda.cudart().cudaHostUnregister(self.buf.data_ptr())
-            self.registered = False
+        rt = torch.cuda.cudart() if getattr(self, "chunks", None) else None
+        for p in getattr(self, "chunks", []):
+            rt.cudaHostUnregister(p)
+        self.chunks = []
+        self.registered = False
 
 
 def layer_bytes(E: int, H: int, I: int) -> int:
