@@ -46,8 +46,7 @@ class SharedHostStore:
     ``group``: torch.distributed process group of the ranks on this machine
     (None for a single process).  ``local_rank`` 0 creates and owns the file."""
 
-    def __init__(self, nbytes: int, local_rank: int = 0, group=None, headroom: int = 8 * GiB,
-                 register: bool = True):
+    def __init__(self, nbytes: int, local_rank: int = 0, group=None, headroom: int = 8 * GiB):
         import torch.distributed as dist
         self.nbytes = nbytes = _align(nbytes)
         self.owner = local_rank == 0
@@ -78,25 +77,34 @@ class SharedHostStore:
             self.fd = os.open(f"/proc/{pid}/fd/{fd}", os.O_RDWR)
         self.mm = mmap.mmap(self.fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
         self.buf = torch.frombuffer(self.mm, dtype=torch.uint8)
-        # Page-lock in 1 GiB pieces: several processes registering one large
-        # range of not-yet-faulted shared pages at the same time was refused
-        # by the OS (cudaErrorOperatingSystem) on this pool, piecewise
-        # registration of the same bytes was not.  Under unified addressing
-        # the pieces map at their host addresses, so a tensor may span two.
         self.chunks = []
-        if register:
-            rt = torch.cuda.cudart()
-            base = self.buf.data_ptr()
-            for off in range(0, nbytes, _CHUNK):
-                n = min(_CHUNK, nbytes - off)
+        self.regions = []          # (offset, bytes) of every take(), registered one by one
+        self.registered = False
+        self._off = 0
+
+    def register(self) -> None:
+        """Page-lock and device-map every region handed out by take(), each as
+        its own registration of at most 1 GiB.  Per-region registration keeps
+        every tensor inside one registration (a copy into a tensor spanning two
+        is rejected), and several processes registering one huge range of
+        not-yet-faulted shared pages at the same time was refused by the OS
+        (cudaErrorOperatingSystem) on this pool while piecewise registration of
+        the same bytes was not.  Call it on the owner before filling, on the
+        other ranks after the owner's fill."""
+        if self.registered:
+            return
+        rt = torch.cuda.cudart()
+        base = self.buf.data_ptr()
+        for off0, nb in self.regions:
+            for off in range(off0, off0 + nb, _CHUNK):
+                n = min(_CHUNK, off0 + nb - off)
                 rc = int(rt.cudaHostRegister(base + off, n, _REGISTER_PORTABLE_MAPPED))
                 if rc != 0:
                     self.close()
                     raise RuntimeError(f"cudaHostRegister of the shared expert store failed "
                                        f"(cudaError {rc}) at offset {off}")
                 self.chunks.append(base + off)
-        self.registered = bool(self.chunks)
-        self._off = 0
+        self.registered = True
 
     def take(self, shape, dtype) -> torch.Tensor:
         """Next page-aligned sub-tensor of the store."""
@@ -107,6 +115,7 @@ class SharedHostStore:
         if self._off + nb > self.nbytes:
             raise ValueError("shared store exhausted")
         t = self.buf[self._off:self._off + nb].view(dtype).view(*shape)
+        self.regions.append((self._off, nb))
         self._off = _align(self._off + nb)
         return t
 

@@ -68,12 +68,19 @@ class OffloadedExperts:
                 self.host.take((experts, hidden, inter), torch.float8_e4m3fn),
                 self.host.take((experts, 2 * inter // 128, hidden // 128), torch.float32),
                 self.host.take((experts, hidden // 128, inter // 128), torch.float32))
-            if self.host.owner:
-                fill_layer(ex, seed + l, self.device, fill)
             self.layers.append(ex)
+        multi = group is not None and dist.is_initialized() and dist.get_world_size(group) > 1
+        # the owner page-locks and fills first; the others page-lock the
+        # already-filled pages after the barrier
+        if self.host.owner:
+            self.host.register()
+            for l, ex in enumerate(self.layers):
+                fill_layer(ex, seed + l, self.device, fill)
         torch.cuda.synchronize(self.device)
-        if group is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
+        if multi:
             dist.barrier(group=group, device_ids=[self.device.index])
+        if not self.host.owner:
+            self.host.register()
         self.setup_s = time.perf_counter() - t0
         for ex in self.layers:
             devcache.init_dev_cache(ex, self.device, capacity, policy=policy)

@@ -25,8 +25,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from drama3_offloading_b200.hoststore import SharedHostStore
-        st = SharedHostStore(1 << 20, local_rank=rank, group=dist.group.WORLD, headroom=0,
-                             register=False)
+        st = SharedHostStore(1 << 20, local_rank=rank, group=dist.group.WORLD, headroom=0)
         a = st.take((256,), torch.int64)
         b = st.take((3, 5), torch.float32)
         if rank == 0:
@@ -68,7 +67,7 @@ def _oom_worker(rank, world, port, q):
     try:
         from drama3_offloading_b200.hoststore import SharedHostStore
         try:
-            SharedHostStore(1 << 60, local_rank=rank, group=dist.group.WORLD, register=False)
+            SharedHostStore(1 << 60, local_rank=rank, group=dist.group.WORLD)
             q.put((rank, "allocated"))
         except MemoryError as exc:
             q.put((rank, "refused" if "available" in str(exc) else repr(exc)))
