@@ -1,0 +1,134 @@
+"""Fully HBM-resident expert-parallel MoE decode.
+
+256 experts per layer are sharded evenly over the N ranks (32 per GPU at
+N = 8) and stay resident in HBM; the global decode batch (64 streams) is
+split over the ranks (64/N tokens each).  Per layer and step, on every rank:
+
+    router (local tokens) -> d3_ep_dispatch_pack (static capacity per peer)
+    -> NCCL all-to-all of the token rows + local expert ids
+    -> d3_moe_fp8_forward over the received rows (one expert per row)
+    -> NCCL all-to-all of the expert outputs back
+    -> d3_ep_combine: h += sum_k w[t,k] y[t,k]
+
+Every buffer has a fixed shape (capacity = local pairs per peer), so the step
+needs no host sync and is captured into one CUDA graph, collectives included.
+At N = 1 the exchange disappears and the layer is one fp8_moe_forward.
+
+No counterpart in the reference (it has no multi-GPU code).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib, moe, synth
+
+
+def exchange(send: torch.Tensor, recv: torch.Tensor, group=None) -> None:
+    """Static all-to-all: row block r of ``send`` goes to rank r, the block
+    from rank r lands in row block r of ``recv`` (equal splits)."""
+    import torch.distributed as dist
+    dist.all_to_all_single(recv, send, group=group)
+
+
+class ExpertParallelMoE:
+    def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048,
+                 inter: int = 512, topk: int = 8, global_batch: int = 64, rank: int = 0,
+                 world: int = 1, group=None, device="cuda", seed: int = 0,
+                 trace: np.ndarray | None = None):
+        if experts % world or global_batch % world:
+            raise ValueError("experts and global_batch must divide evenly over the ranks")
+        self.device = dev = torch.device(device)
+        self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
+        self.rank, self.world, self.group = rank, world, group
+        self.epr = experts // world
+        self.T = global_batch // world
+        self.cap = self.T * topk                    # pairs this rank can send to one peer
+        g = torch.Generator(device=dev).manual_seed(seed + 11)
+        # resident local experts: layer l, global experts [rank*epr, (rank+1)*epr)
+        self.w = [synth.make_experts(self.epr, hidden, inter, seed=seed + 1000 * l + rank,
+                                     device=dev, chunk=16) for l in range(layers)]
+        self.gate = [(torch.randn(experts, hidden, generator=g, device=dev) * 0.02)
+                     .to(torch.bfloat16) for _ in range(layers)]
+        self.h = torch.randn(self.T, hidden, generator=g, device=dev).to(torch.bfloat16)
+        self.ids = torch.empty(self.T, topk, dtype=torch.int32, device=dev)
+        self.wts = torch.empty(self.T, topk, dtype=torch.float32, device=dev)
+        n = world * self.cap
+        self.send_x = torch.zeros(n, hidden, dtype=torch.bfloat16, device=dev)
+        self.recv_x = torch.zeros_like(self.send_x)
+        self.send_eid = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        self.recv_eid = torch.full_like(self.send_eid, -1)
+        self.y = torch.zeros_like(self.send_x)
+        self.ret = torch.zeros_like(self.send_x)
+        self.src_slot = torch.full((self.T, topk), -1, dtype=torch.int32, device=dev)
+        self.ones = torch.ones(n, 1, dtype=torch.float32, device=dev)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+        if trace is None:
+            from .trace import uniform_trace
+            trace = uniform_trace(steps=256, tokens=global_batch, layers=layers,
+                                  experts=experts, k=topk)
+        # this rank's tokens of each step: [steps, layers, T, k]
+        mine = trace[:, :, rank * self.T:(rank + 1) * self.T, :]
+        self.trace_steps = mine.shape[0]
+        self.trace_dev = torch.from_numpy(np.ascontiguousarray(mine).astype(np.int32)).to(dev)
+        self.step_idx = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.graph = None
+        moe.router_topk(self.h, self.gate[0], topk, out_ids=self.ids, out_w=self.wts)
+
+    # ------------------------------------------------------------ one step
+    def _layer(self, l: int, ids: torch.Tensor, gemm_events: list | None = None) -> None:
+        h = self.h
+        moe.router_topk(h, self.gate[l], self.k, out_ids=self.ids, out_w=self.wts)
+        w = self.w[l]
+        if self.world == 1:
+            if gemm_events is not None:
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+            moe.fp8_moe_forward(h, ids, self.wts, w.w13_weight, w.w13_scale_inv, w.w2_weight,
+                                w.w2_scale_inv, out=h, accumulate=True)
+            if gemm_events is not None:
+                e1.record()
+                gemm_events.append((e0, e1))
+            return
+        st = _lib.stream_ptr()
+        _lib.call("d3_ep_dispatch_pack", _lib.ptr(h), _lib.ptr(ids), self.T, self.k, self.H,
+                  self.world, self.epr, self.cap, _lib.ptr(self.send_x), _lib.ptr(self.send_eid),
+                  _lib.ptr(self.src_slot), _lib.ptr(self.overflow), st)
+        exchange(self.send_x, self.recv_x, self.group)
+        exchange(self.send_eid, self.recv_eid, self.group)
+        if gemm_events is not None:
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+        moe.fp8_moe_forward(self.recv_x, self.recv_eid.view(-1, 1), self.ones, w.w13_weight,
+                            w.w13_scale_inv, w.w2_weight, w.w2_scale_inv, out=self.y)
+        if gemm_events is not None:
+            e1.record()
+            gemm_events.append((e0, e1))
+        exchange(self.y, self.ret, self.group)
+        _lib.call("d3_ep_combine", _lib.ptr(self.ret), _lib.ptr(self.src_slot),
+                  _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(h), 1, st)
+
+    def step(self, gemm_events: list | None = None) -> None:
+        cur = self.trace_dev.index_select(0, self.step_idx)[0]
+        self.step_idx.add_(1).remainder_(self.trace_steps)
+        for l in range(self.L):
+            self._layer(l, cur[l], gemm_events)
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.step()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        self.graph = g
+        return g
+
+    def local_expert_bytes(self) -> int:
+        return synth_expert_bytes(self.H, self.I)
+
+
+def synth_expert_bytes(H: int, I: int) -> int:
+    return 3 * H * I + 3 * H * I * 4 // (128 * 128)

@@ -54,5 +54,8 @@ def uniform_trace(steps: int, tokens: int, layers: int = 40, experts: int = 256,
     """Uniform-random top-k without replacement, ``int16 [steps, layers, tokens, k]``
     (the expert-parallel resident configuration routes uniformly)."""
     rng = np.random.default_rng(seed)
-    keys = rng.random((steps, layers, tokens, experts))
-    return np.argsort(keys, axis=-1)[..., :k].astype(np.int16)
+    out = np.empty((steps, layers, tokens, k), dtype=np.int16)
+    for s in range(steps):
+        keys = rng.random((layers, tokens, experts))
+        out[s] = np.argpartition(keys, k - 1, axis=-1)[..., :k]
+    return out

@@ -204,6 +204,30 @@ D3_API int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes,
                               int32_t accumulate, int32_t* err_word, void* workspace,
                               size_t workspace_bytes, d3_stream_t stream);
 
+/* ---------------------------------------------------- expert parallelism */
+
+/* Build the static-capacity all-to-all send buffer for expert parallelism
+ * (experts e in [d*experts_per_rank, (d+1)*experts_per_rank) live on rank d).
+ * Pair (t, j) with expert e = ids[t,j] goes to row d*cap + r of send_x
+ * [n_ranks*cap, H] bf16 (r = its rank among the pairs bound for d, in pair
+ * order) with send_eid[row] = e - d*experts_per_rank; unused rows get -1;
+ * src_slot[t,j] = row (-1 if e is out of range or d's block is full, counted
+ * in *overflow).  cap = T*topk never overflows.  No counterpart in the
+ * reference (it has no multi-GPU path); the resident expert-parallel
+ * configuration of the B200 build. */
+D3_API int d3_ep_dispatch_pack(const void* x, const int32_t* ids, int32_t T, int32_t topk,
+                               int32_t H, int32_t n_ranks, int32_t experts_per_rank, int32_t cap,
+                               void* send_x, int32_t* send_eid, int32_t* src_slot,
+                               int32_t* overflow, d3_stream_t stream);
+
+/* out[t] (+)= sum_j weights[t,j] * ret[src_slot[t,j]] (bf16 rows of H, fixed
+ * j order, skipped where src_slot < 0): the combine after the return
+ * all-to-all.  weights f32 (weights_f32 = 1) or bf16.  No counterpart in the
+ * reference. */
+D3_API int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
+                         int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
+                         int32_t accumulate, d3_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
