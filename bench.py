@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "fetch", "ep"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "fetch", "ep", "prefill"), default="decode")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--global-batch", type=int, default=64, help="ep workload: decode streams")
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--slots", type=int, default=2048, help="fetch workload: slots over all layers")
@@ -325,6 +326,107 @@ def run_fetch(args, rank, world, local):
             "capacity": capacity, "trace": trace, "launches": args.steps * args.layers * 2}
 
 
+# ---------------------------------------------------------------- prefill
+
+def run_prefill(args, rank, world, local):
+    """Prefill gather: a 2048-token bf16 chunk through 40 offloaded layers; per
+    layer the router runs, the union of routed experts (top-8 per token under a
+    Zipf(1.1) prior) is gathered -- cached ones borrowed read-only from the
+    decode cache, the rest fetched from pinned host -- and the token-permuted
+    FP8 grouped GEMM runs on the compact set.  One chunk per step, graph-
+    captured; caches warmed by 64 decode steps of the Zipf trace first."""
+    from drama3_offloading_b200 import benchutil, devcache, moe, offload
+    from drama3_offloading_b200.stack import OffloadedExperts
+    from drama3_offloading_b200.trace import zipf_trace
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T = args.prefill_tokens
+    peak = benchutil.host_link_peak_gbs(device=dev)
+    cap = max(1, int(args.cache_gib * (1 << 30)) // (args.layers * EXPERT_BYTES))
+    store = OffloadedExperts(layers=args.layers, capacity=cap, device=dev, policy=args.policy,
+                             group=local_group(world), local_rank=local)
+    dec = torch.from_numpy(zipf_trace(steps=64, layers=args.layers).astype(np.int32)).to(dev)
+    for s in range(64):
+        for l, ex in enumerate(store.layers):
+            devcache.dev_resolve_and_fetch(ex, dec[s, l])
+    pre = zipf_trace(steps=T, layers=args.layers, seed=1 + rank)       # [T, L, 8]
+    ids = torch.from_numpy(np.ascontiguousarray(pre.transpose(1, 0, 2)).astype(np.int32)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    gate = [(torch.randn(256, 2048, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            for _ in range(args.layers)]
+    h0 = torch.randn(T, 2048, generator=g, device=dev).to(torch.bfloat16)
+    h = h0.clone()
+    wts = torch.empty(T, 8, dtype=torch.float32, device=dev)
+    rids = torch.empty(T, 8, dtype=torch.int32, device=dev)
+
+    def step(events=None):
+        h.copy_(h0)
+        for l, ex in enumerate(store.layers):
+            moe.router_topk(h, gate[l], 8, out_ids=rids, out_w=wts)
+            if events is not None:
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+            y = offload.offloaded_forward(ex, h, ids[l], wts)
+            if events is not None:
+                e1.record()
+                events.append((e0, e1))
+            h.add_(y)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    for _ in range(args.warmup):
+        gr.replay()
+    torch.cuda.synchronize(dev)
+    c0 = [offload.gather_counters(ex) for ex in store.layers]
+    benchutil.barrier(world, dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with benchutil.ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("timed")
+        a.record()
+        for _ in range(args.steps):
+            gr.replay()
+        b.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+    benchutil.barrier(world, dev)
+    ms = benchutil.max_over_ranks(a.elapsed_time(b), world, dev)
+    c1 = [offload.gather_counters(ex) for ex in store.layers]
+    fetched = sum(x["gather_misses"] - y["gather_misses"] for x, y in zip(c1, c0)) / args.steps
+    borrowed = sum(x["gather_hits"] - y["gather_hits"] for x, y in zip(c1, c0)) / args.steps
+    fetch_gbs = fetched * EXPERT_BYTES / (ms / args.steps * 1e-3) / 1e9
+    evs = []
+    step(evs)
+    torch.cuda.synchronize(dev)
+    layer_ms = sum(x.elapsed_time(y) for x, y in evs)
+    flops = T * 8 * 6_291_456 * args.layers
+    return {
+        "metric": "prefill tok/s (2048-token chunk, 40L, offloaded, union gather + FP8 grouped GEMM)",
+        "value": world * T * args.steps / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8 weights x (bf16-class hi/lo fp8 activations)",
+        "data": "synthetic (random-init FP8 experts, Zipf(1.1) top-8 per token)",
+        "config": {"workload": "prefill-gather", "tokens": T, "layers": args.layers,
+                   "cache_slots_per_layer": cap, "parallelism": f"replicas{world}",
+                   "l2": "inputs > L2"},
+        "experts_fetched_per_chunk": fetched, "experts_borrowed_per_chunk": borrowed,
+        "gather_gbs": fetch_gbs, "host_link_peak_gbs": peak["gbs"],
+        "roofline": {"bound": "host_link", "kernel": "gather_kernel (fetch of the union's misses)",
+                     "achieved": fetch_gbs, "peak": peak["gbs"], "unit": "GB/s",
+                     "frac": fetch_gbs / peak["gbs"], "traffic": None},
+        "moe_ms_per_chunk": layer_ms, "moe_tflops": flops / (layer_ms * 1e-3) / 1e12,
+        "clocks": clk.summary(), "gpu_launches": args.steps * args.layers * 9,
+    }
+
+
 # ---------------------------------------------------------------- ep (configs[4])
 
 def run_ep(args, rank, world, local):
@@ -456,8 +558,8 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.workload == "ep":
-        r = run_ep(args, rank, world, local)
+    if args.workload in ("ep", "prefill"):
+        r = (run_ep if args.workload == "ep" else run_prefill)(args, rank, world, local)
         if rank == 0:
             print(json.dumps(r), flush=True)
         if world > 1:

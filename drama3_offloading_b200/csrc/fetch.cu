@@ -314,6 +314,132 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   }
 }
 
+// ---------------------------------------------------------------- prefill gather
+
+// One CTA: which experts a batch routes to.  present[] bitmap in shared memory,
+// a block scan turns it into the ascending expert list and the expert ->
+// compact index map; every pair's id is rewritten to its compact index.
+__global__ void __launch_bounds__(1024) prefill_plan_kernel(const void* ids, int ids_bytes,
+                                                            int n_pairs, int E,
+                                                            int32_t* __restrict__ list,
+                                                            int32_t* __restrict__ n_distinct,
+                                                            int32_t* __restrict__ remap,
+                                                            int32_t* __restrict__ local_ids) {
+  extern __shared__ int32_t s_present[];  // [E]
+  __shared__ int s_warp[32];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += blockDim.x) s_present[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < n_pairs; i += blockDim.x) {
+    const int32_t e = load_id(ids, ids_bytes, i);
+    if (e >= 0 && e < E) s_present[e] = 1;
+  }
+  __syncthreads();
+  // exclusive scan of present[] over contiguous per-thread ranges
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int lo = tid * per, hi = min(E, lo + per);
+  int cnt = 0;
+  for (int e = lo; e < hi; ++e) cnt += s_present[e];
+  int v = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += a;
+  }
+  if (lane == 31) s_warp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int a = lane < (int)(blockDim.x >> 5) ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int b = __shfl_up_sync(0xffffffffu, a, o);
+      if (lane >= o) a += b;
+    }
+    s_warp[lane] = a;
+  }
+  __syncthreads();
+  int pos = (v - cnt) + (warp > 0 ? s_warp[warp - 1] : 0);
+  for (int e = lo; e < hi; ++e) {
+    if (s_present[e]) {
+      list[pos] = e;
+      remap[e] = pos;
+      s_present[e] = pos + 1;  // keep compact index (+1) for the id rewrite
+      ++pos;
+    } else {
+      remap[e] = -1;
+    }
+  }
+  if (tid == 0) *n_distinct = s_warp[31];
+  __syncthreads();
+  for (int i = tid; i < n_pairs; i += blockDim.x) {
+    const int32_t e = load_id(ids, ids_bytes, i);
+    local_ids[i] = (e >= 0 && e < E) ? s_present[e] - 1 : -1;
+  }
+}
+
+struct GatherParams {
+  FetchParams f;                  // host/cache bases and per-buffer sizes (job fields unused)
+  uint4* dst[D3_MAX_BUFFERS];     // compact buffers [n_max][bytes[b]]
+  const int32_t* list;            // experts to gather, compact order
+  const int32_t* n_distinct;
+  const int32_t* slot_of;         // device cache map (read only), or null
+  int32_t num_experts;
+  int64_t* counters;              // {borrowed from cache, fetched from host}, or null
+};
+
+// Flat copy over n_distinct experts x all buffers: a cached expert is read
+// from its device slot (read-only borrow: no stamp, no insert), any other from
+// mapped pinned host memory.
+__global__ void __launch_bounds__(kFetchThreads) gather_kernel(GatherParams p) {
+  pdl_trigger();
+  pdl_wait();
+  const int nd = *p.n_distinct;
+  if (nd <= 0) return;
+  if (blockIdx.x == 0 && threadIdx.x < 32 && p.counters) {
+    int borrowed = 0;
+    for (int j = threadIdx.x; j < nd; j += 32)
+      borrowed += (p.slot_of && p.slot_of[p.list[j]] >= 0) ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) borrowed += __shfl_xor_sync(0xffffffffu, borrowed, o);
+    if (threadIdx.x == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 0), (unsigned long long)borrowed);
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.counters + 1),
+                (unsigned long long)(nd - borrowed));
+    }
+  }
+  const FetchParams& f = p.f;
+  const int64_t total = (int64_t)nd * f.vec_total;
+  constexpr int64_t kChunk = (int64_t)kFetchThreads * kFetchUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * kChunk; base < total;
+       base += (int64_t)gridDim.x * kChunk) {
+    uint4 v[kFetchUnroll];
+    uint4* dptr[kFetchUnroll];
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u) {
+      const int64_t g = base + (int64_t)u * kFetchThreads + threadIdx.x;
+      dptr[u] = nullptr;
+      if (g < total) {
+        const int64_t j = g / f.vec_total;
+        int64_t r = g - j * f.vec_total;
+        int b = 0;
+        while (b < f.nbuf - 1 && r >= f.vecs[b]) { r -= f.vecs[b]; ++b; }
+        const int64_t e = p.list[j];
+        const int s = p.slot_of ? p.slot_of[e] : -1;
+        if (s >= 0)
+          v[u] = f.cache[b][(int64_t)s * f.vecs[b] + r];
+        else
+          v[u] = ld_stream_u4(f.host[b] + e * f.vecs[b] + r);
+        dptr[u] = p.dst[b] + j * f.vecs[b] + r;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u)
+      if (dptr[u]) *dptr[u] = v[u];
+  }
+}
+
 __global__ void lookup_kernel(const int32_t* __restrict__ slot_of, int32_t E, const void* ids,
                               int32_t ids_bytes, int32_t n, int32_t* __restrict__ out) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -525,6 +651,65 @@ int d3_fetch_jobs(const d3_layer_cache* L, int32_t fetch_ctas, d3_stream_t strea
   int rc = make_fetch_params(L, &fp, &expert_bytes);
   if (rc) return rc;
   return launch_fetch(fp, fetch_ctas, (cudaStream_t)stream, false);
+}
+
+int d3_prefill_plan(const void* ids, int32_t ids_bytes, int32_t n_pairs, int32_t num_experts,
+                    int32_t* expert_list, int32_t* n_distinct, int32_t* remap, int32_t* local_ids,
+                    d3_stream_t stream) {
+  D3_CHECK_ARG(ids && expert_list && n_distinct && remap && local_ids,
+               "d3_prefill_plan: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(n_pairs >= 1, "n_pairs must be >= 1");
+  if (num_experts < 1 || num_experts > 16384)
+    return fail(D3_ERR_TOO_LARGE, "num_experts must be in [1, 16384]");
+  const size_t smem = sizeof(int32_t) * (size_t)num_experts;
+  if (smem > 48 * 1024)
+    D3_CUDA_TRY(cudaFuncSetAttribute(prefill_plan_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "prefill plan smem attribute");
+  D3_CUDA_TRY(launch_k(prefill_plan_kernel, dim3(1), dim3(1024), smem, (cudaStream_t)stream,
+                       pdl_enabled(), ids, ids_bytes, n_pairs, num_experts, expert_list,
+                       n_distinct, remap, local_ids),
+              "prefill_plan_kernel launch");
+  return D3_OK;
+}
+
+int d3_gather_experts(const d3_layer_cache* L, const int32_t* expert_list,
+                      const int32_t* n_distinct, void* const* dst, int64_t* counters,
+                      int32_t fetch_ctas, d3_stream_t stream) {
+  D3_CHECK_ARG(L && expert_list && n_distinct && dst, "d3_gather_experts: null pointer");
+  D3_CHECK_ARG(L->nbuf >= 1 && L->nbuf <= D3_MAX_BUFFERS, "nbuf must be in [1, %d]",
+               D3_MAX_BUFFERS);
+  D3_CHECK_ARG(fetch_ctas >= 0 && fetch_ctas <= 65535, "fetch_ctas out of range");
+  GatherParams gp{};
+  int64_t expert_bytes = 0;
+  // a layer without a device cache may pass null cache pointers: nothing is borrowed
+  for (int b = 0; b < L->nbuf; ++b) {
+    D3_CHECK_ARG(L->host[b] && dst[b], "buffer %d: null host or destination pointer", b);
+    if (L->bytes[b] <= 0 || L->bytes[b] % 16)
+      return fail(D3_ERR_MISALIGNED, "buffer %d: bytes per expert %lld not a multiple of 16", b,
+                  (long long)L->bytes[b]);
+    if (!aligned16(L->host[b]) || !aligned16(dst[b]) || (L->cache[b] && !aligned16(L->cache[b])))
+      return fail(D3_ERR_MISALIGNED, "buffer %d: base pointer not 16 B aligned", b);
+    if (L->slot_of) D3_CHECK_ARG(L->cache[b], "buffer %d: slot_of given without a cache", b);
+    gp.f.host[b] = static_cast<const uint4*>(L->host[b]);
+    gp.f.cache[b] = static_cast<uint4*>(L->cache[b]);
+    gp.f.vecs[b] = L->bytes[b] / 16;
+    gp.f.vec_total += gp.f.vecs[b];
+    gp.dst[b] = static_cast<uint4*>(dst[b]);
+    expert_bytes += L->bytes[b];
+  }
+  gp.f.nbuf = L->nbuf;
+  gp.list = expert_list;
+  gp.n_distinct = n_distinct;
+  gp.slot_of = L->slot_of;
+  gp.num_experts = L->num_experts;
+  gp.counters = counters;
+  const int ctas = fetch_ctas > 0 ? fetch_ctas : num_sms();
+  D3_CUDA_TRY(launch_k(gather_kernel, dim3((unsigned)ctas), dim3(kFetchThreads), 0,
+                       (cudaStream_t)stream, pdl_enabled(), gp),
+              "gather_kernel launch");
+  return D3_OK;
 }
 
 int d3_lookup_slots(const int32_t* slot_of, int32_t num_experts, const void* ids,

@@ -1,0 +1,160 @@
+"""Prefill (multi-row) MoE over offloaded experts -- drop-in for the hot-path
+parts of the reference's ``bin/offload.py``.
+
+* ``offloaded_forward(self, x, topk_ids, topk_weights)`` (bin/offload.py:137-239):
+  the distinct routed experts of the batch are gathered into a compact device
+  buffer -- cached ones copied read-only from the device cache (the reference's
+  HYBRID_GATHER borrow, :195-224: no stamp bump, no insert), the rest fetched
+  from pinned host memory -- then the FP8 grouped GEMM runs on the compact set
+  with the ids remapped.  Unlike the reference (``torch.unique(ids.cpu())``, a
+  host sync per layer, then one ``copy_`` per expert and buffer), the union,
+  the remap and the gather are three device launches with static shapes.
+* ``STATS``, ``HYBRID_GATHER``, ``GATHER_DONE_HOOK``, ``EXPERT_BYTES``,
+  ``pin_experts``, ``size_cache_to_free_vram``, ``install_offload`` keep the
+  reference's names and meaning (:242-254, :603-704).
+
+Gather counts are kept on the device (``gather_counters(experts)``) rather
+than as host-side STATS increments, which would need a sync.
+"""
+from __future__ import annotations
+
+import ctypes
+import time
+
+import torch
+
+from . import _lib, moe
+
+EXPERT_BYTES = 3_146_496
+HYBRID_GATHER = True
+GATHER_DONE_HOOK = None
+ACTIVATION_HEADROOM_GIB = 1.5
+STATS = {"experts_copied": 0, "bytes_copied": 0, "hits": 0, "misses": 0,
+         "gather_hits": 0, "gather_misses": 0}
+
+_BUF: dict = {}
+
+
+def _buffers(experts, device):
+    """Compact gather buffers for every expert of the layer shape, plus the plan
+    tables; allocated once per (device, shape) and reused by every layer."""
+    key = (device.index, tuple(experts.w13_weight.shape), tuple(experts.w2_weight.shape))
+    b = _BUF.get(key)
+    if b is None:
+        E = experts.num_experts
+        b = {
+            "w13": torch.empty_like(experts.w13_weight, device=device),
+            "w2": torch.empty_like(experts.w2_weight, device=device),
+            "s13": torch.empty(experts.w13_scale_inv.shape, dtype=torch.float32, device=device),
+            "s2": torch.empty(experts.w2_scale_inv.shape, dtype=torch.float32, device=device),
+            "list": torch.empty(E, dtype=torch.int32, device=device),
+            "n": torch.zeros(1, dtype=torch.int32, device=device),
+            "remap": torch.empty(E, dtype=torch.int32, device=device),
+        }
+        b["dst"] = (ctypes.c_void_p * 4)(*(b[n].data_ptr() for n in ("w13", "w2", "s13", "s2")))
+        _BUF[key] = b
+    return b
+
+
+def _layer_desc(experts):
+    """The layer's device-cache descriptor, or a host-only one (no cache)."""
+    d = getattr(experts, "_dc_desc", None)
+    if d is not None and HYBRID_GATHER:
+        return d
+    from .devcache import _BUFFERS, _host_device_ptr
+    hd = getattr(experts, "_d3_host_only_desc", None)
+    if hd is None:
+        hd = _lib.LayerCache()
+        hd.num_experts = experts.num_experts
+        hd.nbuf = 4
+        for b, name in enumerate(_BUFFERS):
+            t = getattr(experts, name)
+            hd.host[b] = _host_device_ptr(t)
+            hd.bytes[b] = t.numel() * t.element_size() // experts.num_experts
+        experts._d3_host_only_desc = hd
+    return hd
+
+
+def gather_counters(experts) -> dict:
+    c = getattr(experts, "_d3_gather_counters", None)
+    if c is None:
+        return {"gather_hits": 0, "gather_misses": 0}
+    v = c.tolist()
+    return {"gather_hits": v[0], "gather_misses": v[1]}
+
+
+def offloaded_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
+    """MoE forward for experts held in pinned host memory (any number of rows)."""
+    if self.w13_weight.device.type != "cpu":
+        return moe.fp8_moe_forward(x, topk_ids, topk_weights, self.w13_weight,
+                                   self.w13_scale_inv, self.w2_weight, self.w2_scale_inv)
+    device = x.device
+    T, k = topk_ids.shape
+    E = self.num_experts
+    b = _buffers(self, device)
+    ids = topk_ids.reshape(-1)
+    if ids.dtype not in (torch.int32, torch.int64):
+        ids = ids.to(torch.int32)
+    ids = ids.contiguous()
+    local = torch.empty(T, k, dtype=torch.int32, device=device)
+    st = _lib.stream_ptr()
+    _lib.call("d3_prefill_plan", _lib.ptr(ids), ids.element_size(), ids.numel(), E,
+              _lib.ptr(b["list"]), _lib.ptr(b["n"]), _lib.ptr(b["remap"]), _lib.ptr(local), st)
+    cnt = getattr(self, "_d3_gather_counters", None)
+    if cnt is None:
+        cnt = torch.zeros(2, dtype=torch.int64, device=device)
+        self._d3_gather_counters = cnt
+    _lib.call("d3_gather_experts", ctypes.byref(_layer_desc(self)), _lib.ptr(b["list"]),
+              _lib.ptr(b["n"]), b["dst"], _lib.ptr(cnt), int(fetch_ctas), st)
+    if GATHER_DONE_HOOK is not None:
+        GATHER_DONE_HOOK()
+    return moe.fp8_moe_forward(x, local, topk_weights, b["w13"], b["s13"], b["w2"], b["s2"])
+
+
+def pin_experts(model, device=None) -> tuple[float, float]:
+    """Page-lock the CPU-resident expert buffers (bin/offload.py:664-699).
+    Returns (GiB, seconds)."""
+    started = time.perf_counter()
+    total = 0
+    for layer in model.backbone.model.layers:
+        experts = getattr(layer.mlp, "experts", None)
+        if experts is None or experts.w13_weight.device.type != "cpu":
+            continue
+        for name in ("w13_weight", "w2_weight", "w13_scale_inv", "w2_scale_inv"):
+            buf = getattr(experts, name)
+            if buf.is_pinned():
+                continue
+            pinned = buf.pin_memory()
+            setattr(experts, name, pinned)
+            total += pinned.numel() * pinned.element_size()
+    return total / 2**30, time.perf_counter() - started
+
+
+def size_cache_to_free_vram(model, device, leave_free_gib: float = 2.0,
+                            cap_per_layer: int = 256) -> int:
+    """Per-layer device-cache capacity from the memory free right now
+    (bin/offload.py:611-661); allocates the caches and returns the capacity."""
+    from . import devcache
+    layers = [l.mlp.experts for l in model.backbone.model.layers
+              if getattr(l.mlp, "experts", None) is not None
+              and l.mlp.experts.w13_weight.device.type == "cpu"]
+    if not layers:
+        return 0
+    torch.cuda.synchronize(device)
+    torch.cuda.empty_cache()
+    free, _ = torch.cuda.mem_get_info(device)
+    budget = free - int((leave_free_gib + ACTIVATION_HEADROOM_GIB) * 2**30)
+    capacity = int(max(0, budget) // (len(layers) * EXPERT_BYTES))
+    capacity = min(capacity, cap_per_layer, layers[0].num_experts)
+    if capacity <= 0:
+        return 0
+    for experts in layers:
+        devcache.init_dev_cache(experts, device, capacity)
+    return capacity
+
+
+def install_offload(experts_cls) -> None:
+    """Route ``experts_cls.forward`` through offloaded_forward, keeping the
+    stock forward as ``_stock_forward`` (bin/offload.py:702-704)."""
+    experts_cls._stock_forward = experts_cls.forward
+    experts_cls.forward = offloaded_forward

@@ -139,6 +139,28 @@ D3_API int d3_fetch_jobs(const d3_layer_cache* layer, int32_t fetch_ctas, d3_str
 D3_API int d3_lookup_slots(const int32_t* slot_of, int32_t num_experts, const void* ids,
                     int32_t ids_bytes, int32_t n, int32_t* slot_out, d3_stream_t stream);
 
+/* Prefill plan, without a host sync: the distinct experts a batch routes to.
+ * expert_list[0..*n_distinct) = those experts ascending, remap[e] = their
+ * compact index (-1 if unused), local_ids[i] = remap[ids[i]] (-1 for
+ * out-of-range ids).  One launch.
+ * Replaces torch.unique(topk_ids.cpu(), return_inverse=True) of the gather
+ * path -- bin/offload.py:157-158 (a host sync per layer). */
+D3_API int d3_prefill_plan(const void* ids, int32_t ids_bytes, int32_t n_pairs,
+                           int32_t num_experts, int32_t* expert_list, int32_t* n_distinct,
+                           int32_t* remap, int32_t* local_ids, d3_stream_t stream);
+
+/* Gather the experts of expert_list[0..*n_distinct) into compact buffers
+ * dst[b] ([n_max][layer->bytes[b]]) in one launch: an expert resident in the
+ * layer's device cache (layer->slot_of[e] >= 0) is copied from its slot --
+ * read-only, no stamp or insert -- any other is read from the pinned host
+ * store.  counters (optional, int64[2]) accumulate {borrowed, fetched}.
+ * layer->slot_of may be NULL (no cache: everything from host).
+ * Replaces the hybrid gather of offloaded_forward -- bin/offload.py:186-226
+ * (per-expert copy_ calls plus index copies of the scales). */
+D3_API int d3_gather_experts(const d3_layer_cache* layer, const int32_t* expert_list,
+                             const int32_t* n_distinct, void* const* dst, int64_t* counters,
+                             int32_t fetch_ctas, d3_stream_t stream);
+
 /* ------------------------------------------------------------------ router */
 
 /* Workspace bytes d3_router_topk needs for T tokens and E experts. */

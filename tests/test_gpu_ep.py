@@ -49,7 +49,8 @@ def test_dispatch_pack_and_combine(n_ranks, T, k, cap):
     # combine of arbitrary returned rows
     ret = torch.randn(n_ranks * cap, H, generator=g).to(torch.bfloat16)
     out = torch.zeros(T, H, dtype=torch.bfloat16, device=DEV)
-    _lib.call("d3_ep_combine", _lib.ptr(ret.to(DEV)), _lib.ptr(src), _lib.ptr(w.to(DEV)), 1, T,
+    ret_d, w_d = ret.to(DEV), w.to(DEV)   # kept alive until the kernel has run
+    _lib.call("d3_ep_combine", _lib.ptr(ret_d), _lib.ptr(src), _lib.ptr(w_d), 1, T,
               k, H, _lib.ptr(out), 0, _lib.stream_ptr())
     torch.cuda.synchronize()
     want = ref.combine(ret, want_src, w)

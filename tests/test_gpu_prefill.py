@@ -1,0 +1,120 @@
+"""Prefill gather on the GPU, through the C ABI: the device-side union/remap
+(replacing torch.unique(ids.cpu()), bin/offload.py:157-158), the one-launch
+hybrid gather (cached experts borrowed read-only from the device cache, the
+rest fetched from pinned host, bin/offload.py:186-226) with self-identifying
+bytes, and offloaded_forward against the all-resident path and the oracle."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import cuda_available
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not cuda_available(), reason="needs a CUDA GPU")]
+
+from drama3_offloading_b200 import _lib, devcache, moe, offload, synth  # noqa: E402
+
+DEV = torch.device("cuda:0")
+
+
+def test_prefill_plan_matches_unique():
+    g = torch.Generator().manual_seed(5)
+    E = 256
+    ids = torch.randint(0, E, (300, 8), generator=g, dtype=torch.int32)
+    ids[0, 0] = -1
+    ids[1, 1] = E + 3
+    d = ids.to(DEV)
+    lst = torch.empty(E, dtype=torch.int32, device=DEV)
+    n = torch.zeros(1, dtype=torch.int32, device=DEV)
+    remap = torch.empty(E, dtype=torch.int32, device=DEV)
+    local = torch.empty_like(d)
+    _lib.call("d3_prefill_plan", _lib.ptr(d), 4, d.numel(), E, _lib.ptr(lst), _lib.ptr(n),
+              _lib.ptr(remap), _lib.ptr(local), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    flat = ids.reshape(-1).numpy()
+    valid = flat[(flat >= 0) & (flat < E)]
+    uniq = np.unique(valid)
+    assert int(n.item()) == len(uniq)
+    np.testing.assert_array_equal(lst.cpu().numpy()[:len(uniq)], uniq)
+    want_remap = np.full(E, -1)
+    want_remap[uniq] = np.arange(len(uniq))
+    np.testing.assert_array_equal(remap.cpu().numpy(), want_remap)
+    want_local = np.where((flat >= 0) & (flat < E), want_remap[np.clip(flat, 0, E - 1)], -1)
+    np.testing.assert_array_equal(local.cpu().numpy().reshape(-1), want_local)
+
+
+@pytest.fixture(scope="module")
+def pattern_host():
+    return synth.pattern_experts(64)
+
+
+def test_gather_borrows_read_only_and_fetches_misses(pattern_host):
+    ex = synth.HostExperts(64, pattern_host.w13_weight, pattern_host.w2_weight,
+                           pattern_host.w13_scale_inv, pattern_host.w2_scale_inv)
+    devcache.init_dev_cache(ex, DEV, 16)
+    # make experts 0..7 resident
+    devcache.dev_resolve_and_fetch(ex, torch.arange(8, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    stamp0 = ex._dc_stamp.clone()
+    step0 = ex._dc_step.clone()
+    slot_of0 = ex._dc_slot_of.clone()
+    ids = torch.tensor([[3, 40, 5], [40, 12, 63], [0, 5, 12]], dtype=torch.int32, device=DEV)
+    x = torch.randn(3, 2048, device=DEV).to(torch.bfloat16)
+    b = offload._buffers(ex, DEV)
+    offload.offloaded_forward  # noqa: B018 (the function under test below uses these)
+    lst = b["list"]
+    local = torch.empty_like(ids)
+    st = _lib.stream_ptr()
+    _lib.call("d3_prefill_plan", _lib.ptr(ids), 4, ids.numel(), 64, _lib.ptr(lst),
+              _lib.ptr(b["n"]), _lib.ptr(b["remap"]), _lib.ptr(local), st)
+    cnt = torch.zeros(2, dtype=torch.int64, device=DEV)
+    _lib.call("d3_gather_experts", ctypes.byref(ex._dc_desc), _lib.ptr(lst), _lib.ptr(b["n"]),
+              b["dst"], _lib.ptr(cnt), 0, st)
+    torch.cuda.synchronize()
+    uniq = [0, 3, 5, 12, 40, 63]
+    assert int(b["n"].item()) == len(uniq)
+    assert lst[:len(uniq)].tolist() == uniq
+    assert cnt.tolist() == [3, 3]  # 0, 3, 5 borrowed; 12, 40, 63 fetched
+    for bi, name in enumerate(("w13", "w2", "s13", "s2")):
+        v = b[name].view(torch.uint8).reshape(64, -1).view(torch.int64)
+        kk = torch.arange(v.shape[1], dtype=torch.int64, device=DEV)
+        for j, e in enumerate(uniq):
+            assert torch.equal(v[j], kk + ((bi << 56) | (e << 32))), (name, j, e)
+    # read-only: the cache tables did not move
+    assert torch.equal(ex._dc_stamp, stamp0)
+    assert torch.equal(ex._dc_step, step0)
+    assert torch.equal(ex._dc_slot_of, slot_of0)
+    del x
+
+
+@pytest.mark.parametrize("T,cap", [(64, 16), (300, 32), (5, 0)])
+def test_offloaded_forward_equals_resident(T, cap):
+    E = 64
+    ref = synth.make_experts(E, seed=9, device="cuda")
+    host = ref.to("cpu").pin()
+    if cap:
+        devcache.init_dev_cache(host, DEV, cap)
+        devcache.dev_resolve_and_fetch(host, torch.randperm(E)[:8].to(DEV))
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    ids = torch.stack([torch.randperm(E, generator=g)[:8] for _ in range(T)]).to(DEV)
+    w = torch.rand(T, 8, generator=g)
+    w = (w / w.sum(-1, keepdim=True)).to(DEV)
+    want = moe.fp8_moe_forward(x, ids, w, ref.w13_weight, ref.w13_scale_inv, ref.w2_weight,
+                               ref.w2_scale_inv).clone()
+    got = offload.offloaded_forward(host, x, ids, w)
+    moe.check_errors(DEV)
+    assert torch.equal(got, want)
+    if T <= 64:
+        cpu = ref.to("cpu")
+        o = oracle.moe_forward(x.cpu(), ids.cpu(), w.cpu(), cpu.w13_weight, cpu.w13_scale_inv,
+                               cpu.w2_weight, cpu.w2_scale_inv)
+        err = float((got.float().cpu() - o).abs().max() / o.abs().max())
+        assert err < 1e-2, err
+    # dev_cached_forward sends multi-row batches down this path
+    if cap:
+        got2 = devcache.dev_cached_forward(host, x, ids, w)
+        assert torch.equal(got2, want)
