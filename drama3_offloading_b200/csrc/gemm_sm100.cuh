@@ -1,0 +1,295 @@
+// Block-scaled FP8 grouped GEMM tile engine for sm_100a (tcgen05 + TMEM + TMA).
+//
+// One persistent CTA per SM walks a device-built tile list.  A tile is
+// (expert e, 128-row M block m of the expert's weight, N block of BN routed
+// pairs starting at sorted row row0, K-block range [kb0, kb1)).  Swap-AB: the
+// weight rows are the MMA's M (128) and the pairs its N, so a single decode
+// token still drives full-height MMAs.
+//
+// Warp roles (THREADS = 64 + 32*EPI):
+//   warp 0     TMA producer (one elected lane): per pipeline stage KPS
+//              consecutive K-blocks of the weight tile (KPS x 128x128 B, 128 B
+//              swizzle) and of the activation hi/lo planes (2 x KPS x BNx128 B).
+//              Loading K-block pairs back to back asks DRAM for 256 contiguous
+//              bytes of every weight row at once instead of two 128-B halves
+//              a stage apart.
+//   warp 1     MMA issuer (one lane): per K-block, 4 MMAs (K = 32 each) against
+//              hi and 4 against lo into one TMEM accumulator (so D = W.(hi+lo)),
+//              accumulators double-buffered, tcgen05.commit -> mbarriers.
+//   warps 2..  epilogue: each thread owns one accumulator row (TMEM lane) and
+//              CPT columns; per K-block it reads the accumulator and adds
+//              scale[kb][n] * D into fp32 registers (per-block promotion, the
+//              128x128 weight scale times the activation block scale); the
+//              per-tile scales are staged once in shared memory, weight scale
+//              folded in.  At tile end the fp32 partial sums are stored to the
+//              split-K workspace (coalesced across the 32 rows of a warp).
+// Every mbarrier wait is bounded by the global timer; on expiry the CTA
+// records an error word, unwinds, waits for its own MMAs and frees TMEM.
+#pragma once
+
+#include "d3_common.cuh"
+
+#include <cuda.h>
+
+namespace d3 {
+
+constexpr uint64_t kGemmWaitBudgetNs = 2000000000ull;  // 2 s per wait, then abort
+constexpr int kGemmMaxTileKb = 32;                     // K-blocks one tile may span
+
+struct GemmParams {
+  const int4* tiles;
+  const int* ntiles;          // device count of valid tiles
+  const float* wscale;        // [n][mblocks][kblocks]
+  int rows_per_expert;        // weight rows per expert (2I or H)
+  int mblocks, kblocks;       // per expert, 128-granular
+  const float* xscale;        // [rows][kblocks] activation block scales
+  int K;                      // bytes per weight row = K elements
+  float* out;                 // [split][P][Mtot]
+  int P, Mtot, kbps;
+  int* err;                   // device error word (first failure wins)
+};
+
+template <int BN, int KPS>
+struct GemmCfg {
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int KB_BYTES = A_BYTES + 2 * B_BYTES;   // one K-block
+  static constexpr int STAGE_BYTES = KPS * KB_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  static constexpr int EPI = BN >= 64 ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI;
+  static constexpr int CPT = BN * 4 / EPI;
+  static constexpr int SCALE_BYTES = kGemmMaxTileKb * BN * 4;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + SCALE_BYTES + 256;
+  static_assert(STAGES >= 2, "pipeline needs at least two stages");
+};
+
+__device__ __forceinline__ void gemm_error(int* err, int code) { atomicCAS(err, 0, code); }
+
+__device__ __forceinline__ void epi_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+template <int BN, int KPS>
+__global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_x, GemmParams p) {
+  using Cfg = GemmCfg<BN, KPS>;
+  constexpr int S = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint8_t* stage_base = smem;
+  float* s_scale = reinterpret_cast<float*>(smem + (size_t)S * Cfg::STAGE_BYTES);  // [kb][BN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * Cfg::STAGE_BYTES +
+                                               Cfg::SCALE_BYTES);
+  uint64_t* full = bars;             // [S]
+  uint64_t* empty = bars + S;        // [S]
+  uint64_t* accf = bars + 2 * S;     // [2]
+  uint64_t* acce = bars + 2 * S + 2; // [2]
+  uint64_t* done = bars + 2 * S + 4; // [1]
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(accf + i, 1); mbar_init(acce + i, 32 * Cfg::EPI); }
+    mbar_init(done, 1);
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  // everything above is CTA-local set-up that overlaps the previous launch;
+  // the tile list and operands are produced upstream
+  pdl_trigger();
+  pdl_wait();
+  const int ntiles = *p.ntiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+        const int4 tl = p.tiles[t];
+        const int e = tl.x, m = tl.y, row0 = tl.z;
+        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+        const int wrow = e * p.rows_per_expert + m * 128;
+        for (int kb = kb0; kb < kb1; kb += KPS) {
+          if (!mbar_wait(empty + stage, phase ^ 1, kGemmWaitBudgetNs)) {
+            gemm_error(p.err, 1); s_abort = 1; break;
+          }
+          const int nk = min(KPS, kb1 - kb);
+          uint8_t* st = stage_base + (size_t)stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(full + stage, nk * Cfg::KB_BYTES);
+          for (int q = 0; q < nk; ++q) {
+            uint8_t* a = st + q * Cfg::KB_BYTES;
+            tma_load_2d(a, &tm_w, full + stage, (kb + q) * 128, wrow);
+          }
+          for (int q = 0; q < nk; ++q) {
+            uint8_t* bh = st + q * Cfg::KB_BYTES + Cfg::A_BYTES;
+            tma_load_2d(bh, &tm_x, full + stage, (kb + q) * 128, row0);
+            tma_load_2d(bh + Cfg::B_BYTES, &tm_x, full + stage, p.K + (kb + q) * 128, row0);
+          }
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t it = 0;  // accumulator use counter (one per K-block)
+      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+        const int4 tl = p.tiles[t];
+        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1 && ok; kb += KPS) {
+          if (!mbar_wait(full + stage, phase, kGemmWaitBudgetNs)) {
+            gemm_error(p.err, 2); s_abort = 1; break;
+          }
+          const int nk = min(KPS, kb1 - kb);
+          const uint32_t st = smem_u32(stage_base + (size_t)stage * Cfg::STAGE_BYTES);
+          for (int q = 0; q < nk; ++q, ++it) {
+            const uint32_t ab = it & 1, aph = (it >> 1) & 1;
+            if (!mbar_wait(acce + ab, aph ^ 1, kGemmWaitBudgetNs)) {
+              gemm_error(p.err, 2); s_abort = 1; ok = false; break;
+            }
+            tc_fence_after();
+            const uint32_t a = st + q * Cfg::KB_BYTES;
+            const uint32_t bh = a + Cfg::A_BYTES, bl = bh + Cfg::B_BYTES;
+            const uint32_t d = tmem + ab * BN;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bh + kk * 32), idesc,
+                         kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bl + kk * 32), idesc, 1u);
+            mma_commit(accf + ab);
+          }
+          if (!ok) break;
+          mma_commit(empty + stage);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      // every issued MMA has retired before TMEM is released
+      if (it > 0) {
+        mma_commit(done);
+        if (!mbar_wait(done, 0, kGemmWaitBudgetNs)) gemm_error(p.err, 3);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM lane quadrant = warp % 4, column group
+    constexpr int CPT = Cfg::CPT;
+    constexpr int NEPI = 32 * Cfg::EPI;
+    const int ep = threadIdx.x - 64;                // 0 .. NEPI-1
+    const int q = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * CPT;
+    const int row = q * 32 + lane;                 // weight row within the M tile
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + col0;
+    __shared__ int s_tile_abort;
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int4 tl = p.tiles[t];
+      const int e = tl.x, m = tl.y, row0 = tl.z;
+      const int ncount = tl.w & 0xFF;
+      const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+      const int nkb = kb1 - kb0;
+      // stage this tile's promotion scales: scale[j][n] = s_w[kb0+j] * s_x[row0+n][kb0+j]
+      epi_bar_sync(NEPI);  // every epilogue thread is done with the previous tile's scales
+      if (ep == 0) s_tile_abort = s_abort;
+      const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
+      for (int i = ep; i < nkb * BN; i += NEPI) {
+        const int j = i / BN, n = i - j * BN;
+        s_scale[i] = n < ncount
+                         ? __ldg(ws + kb0 + j) *
+                               __ldg(p.xscale + (size_t)(row0 + n) * p.kblocks + kb0 + j)
+                         : 0.f;
+      }
+      epi_bar_sync(NEPI);
+      // the abort decision is taken once per tile from one shared word, so all
+      // epilogue threads leave together (none is left waiting at a barrier)
+      if (s_tile_abort) break;
+      float r[CPT];
+#pragma unroll
+      for (int n = 0; n < CPT; ++n) r[n] = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nkb; ++j, ++it) {
+        const uint32_t ab = it & 1, aph = (it >> 1) & 1;
+        if (!ok) continue;
+        if (!mbar_wait(accf + ab, aph, kGemmWaitBudgetNs)) {
+          gemm_error(p.err, 4); s_abort = 1; ok = false; continue;
+        }
+        tc_fence_after();
+        const float4* sc = reinterpret_cast<const float4*>(s_scale + j * BN + col0);
+#pragma unroll
+        for (int c16 = 0; c16 < CPT / 16; ++c16) {
+          uint32_t v[16];
+          tmem_ld16(lane_base + ab * BN + c16 * 16, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const float4 s4 = sc[c16 * 4 + c4];
+            const int n = c16 * 16 + c4 * 4;
+            r[n + 0] = fmaf(s4.x, __uint_as_float(v[c4 * 4 + 0]), r[n + 0]);
+            r[n + 1] = fmaf(s4.y, __uint_as_float(v[c4 * 4 + 1]), r[n + 1]);
+            r[n + 2] = fmaf(s4.z, __uint_as_float(v[c4 * 4 + 2]), r[n + 2]);
+            r[n + 3] = fmaf(s4.w, __uint_as_float(v[c4 * 4 + 3]), r[n + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acce + ab);
+      }
+      if (!ok) continue;  // leaves at the next tile's shared abort decision
+      const int split = kb0 / p.kbps;
+      float* o = p.out + ((size_t)split * p.P + row0 + col0) * p.Mtot + m * 128 + row;
+#pragma unroll
+      for (int n = 0; n < CPT; ++n)
+        if (col0 + n < ncount) o[(size_t)n * p.Mtot] = r[n];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+template <int BN, int KPS>
+static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& gp,
+                       int max_tiles, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, KPS>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    D3_CUDA_TRY(cudaFuncSetAttribute(moe_gemm_kernel<BN, KPS>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM),
+                "gemm smem attribute");
+    attr_set[dev] = true;
+  }
+  int grid = num_sms();
+  if (max_tiles < grid) grid = max_tiles;
+  if (grid < 1) grid = 1;
+  D3_CUDA_TRY(launch_k(moe_gemm_kernel<BN, KPS>, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st,
+                       pdl_enabled(), tw, tx, gp),
+              "moe_gemm_kernel launch");
+  return D3_OK;
+}
+
+}  // namespace d3

@@ -30,6 +30,7 @@
 // still runs full-height MMAs.  The GEMMs stream each weight byte from HBM
 // once per N tile; K-splits spread a small batch's few experts over all SMs.
 #include "d3_common.cuh"
+#include "gemm_sm100.cuh"
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -83,7 +84,6 @@ static int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_
 
 constexpr int kMaxExperts = 8192;
 constexpr int kMaxPairs = 65536;
-constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s per wait, then abort
 
 struct Plan {
   int P;        // routed pairs = T * topk
@@ -115,6 +115,7 @@ static void make_plan(Plan& p, int T, int topk, int n, int H, int I, int sms) {
     if (want < 1) want = 1;
     if (want > nkb) want = nkb;
     kbps = (nkb + want - 1) / want;
+    if (kbps > kGemmMaxTileKb) kbps = kGemmMaxTileKb;  // a tile's scales fit shared memory
     split = (nkb + kbps - 1) / kbps;
   };
   split_for(2 * I / 128, H / 128, p.split1, p.kbps1);
@@ -416,222 +417,7 @@ __global__ void combine_kernel(const float* __restrict__ ws2, int split, int P, 
 }
 
 // ---------------------------------------------------------------- 3/5. GEMM
-
-struct GemmParams {
-  const int4* tiles;
-  const int* ntiles;          // device count of valid tiles
-  const float* wscale;        // [n][mblocks][kblocks]
-  int rows_per_expert;        // weight rows per expert (2I or H)
-  int mblocks, kblocks;       // per expert, 128-granular
-  const float* xscale;        // [P][kblocks]
-  int K;                      // bytes per weight row = K elements
-  float* out;                 // [split][P][Mtot]
-  int P, Mtot, kbps;
-  int* err;                   // device error word (first failure wins)
-};
-
-template <int BN>
-struct GemmCfg {
-  static constexpr int A_BYTES = 128 * 128;
-  static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGES = BN <= 16 ? 8 : 6;
-  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;  // power of two for 16/64
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
-  // warp 0 TMA, warp 1 MMA, then EPI epilogue warps; each epilogue thread owns
-  // one accumulator row (TMEM lane) and CPT of the BN columns
-  static constexpr int EPI = BN >= 64 ? 8 : 4;
-  static constexpr int THREADS = 64 + 32 * EPI;
-  static constexpr int CPT = BN * 4 / EPI;
-};
-
-__device__ __forceinline__ void gemm_error(int* err, int code) { atomicCAS(err, 0, code); }
-
-template <int BN>
-__global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
-                    const __grid_constant__ CUtensorMap tm_x, GemmParams p) {
-  using Cfg = GemmCfg<BN>;
-  constexpr int S = Cfg::STAGES;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  uint8_t* stage_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * Cfg::STAGE_BYTES);
-  uint64_t* full = bars;             // [S]
-  uint64_t* empty = bars + S;        // [S]
-  uint64_t* accf = bars + 2 * S;     // [2]
-  uint64_t* acce = bars + 2 * S + 2; // [2]
-  uint64_t* done = bars + 2 * S + 4; // [1]
-  __shared__ uint32_t s_tmem;
-  __shared__ volatile int s_abort;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(accf + i, 1); mbar_init(acce + i, 32 * Cfg::EPI); }
-    mbar_init(done, 1);
-    s_abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_x);
-  }
-  if (warp == 1) {
-    tmem_alloc(&s_tmem, Cfg::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s_tmem;
-  // everything above is CTA-local set-up that overlaps the previous launch;
-  // the tile list and operands are produced upstream
-  pdl_trigger();
-  pdl_wait();
-  const int ntiles = *p.ntiles;
-
-  if (warp == 0) {
-    // ---------------- TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
-        const int4 tl = p.tiles[t];
-        const int e = tl.x, m = tl.y, row0 = tl.z;
-        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
-        const int wrow = e * p.rows_per_expert + m * 128;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(empty + stage, phase ^ 1, kWaitBudgetNs)) {
-            gemm_error(p.err, 1); s_abort = 1; break;
-          }
-          uint8_t* a = stage_base + (size_t)stage * Cfg::STAGE_BYTES;
-          uint8_t* bh = a + Cfg::A_BYTES;
-          uint8_t* bl = bh + Cfg::B_BYTES;
-          mbar_arrive_expect_tx(full + stage, Cfg::STAGE_BYTES);
-          tma_load_2d(a, &tm_w, full + stage, kb * 128, wrow);
-          tma_load_2d(bh, &tm_x, full + stage, kb * 128, row0);
-          tma_load_2d(bl, &tm_x, full + stage, p.K + kb * 128, row0);
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t it = 0;  // accumulator use counter
-      for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
-        const int4 tl = p.tiles[t];
-        const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t ab = it & 1, aph = (it >> 1) & 1;
-          if (!mbar_wait(acce + ab, aph ^ 1, kWaitBudgetNs) ||
-              !mbar_wait(full + stage, phase, kWaitBudgetNs)) {
-            gemm_error(p.err, 2); s_abort = 1; break;
-          }
-          tc_fence_after();
-          const uint32_t a = smem_u32(stage_base + (size_t)stage * Cfg::STAGE_BYTES);
-          const uint32_t bh = a + Cfg::A_BYTES, bl = bh + Cfg::B_BYTES;
-          const uint32_t d = tmem + ab * BN;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bh + kk * 32), idesc,
-                       kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8f6f4(d, smem_desc_k128(a + kk * 32), smem_desc_k128(bl + kk * 32), idesc, 1u);
-          mma_commit(empty + stage);
-          mma_commit(accf + ab);
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-      }
-      // every issued MMA has retired before TMEM is released
-      if (it > 0) {
-        mma_commit(done);
-        if (!mbar_wait(done, 0, kWaitBudgetNs)) gemm_error(p.err, 3);
-      }
-    }
-  } else {
-    // ---------------- epilogue: TMEM lane quadrant = warp % 4, column group
-    constexpr int CPT = Cfg::CPT;
-    const int q = warp & 3;
-    const int col0 = ((warp - 2) >> 2) * CPT;
-    const int row = q * 32 + lane;                 // weight row within the M tile
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + col0;
-    uint32_t it = 0;
-    for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
-      const int4 tl = p.tiles[t];
-      const int e = tl.x, m = tl.y, row0 = tl.z;
-      const int ncount = tl.w & 0xFF;
-      const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
-      float r[CPT];
-#pragma unroll
-      for (int n = 0; n < CPT; ++n) r[n] = 0.f;
-      const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const uint32_t ab = it & 1, aph = (it >> 1) & 1;
-        if (!mbar_wait(accf + ab, aph, kWaitBudgetNs)) {
-          gemm_error(p.err, 4); s_abort = 1; ok = false; break;
-        }
-        tc_fence_after();
-        const float sw = __ldg(ws + kb);
-#pragma unroll
-        for (int j = 0; j < CPT / 16; ++j) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + ab * BN + j * 16, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int n = j * 16 + c;
-            const float sx = col0 + n < ncount
-                                 ? __ldg(p.xscale + (size_t)(row0 + col0 + n) * p.kblocks + kb)
-                                 : 0.f;
-            r[n] = fmaf(sw * sx, __uint_as_float(v[c]), r[n]);
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(acce + ab);
-      }
-      if (!ok) break;
-      const int split = kb0 / p.kbps;
-      float* o = p.out + ((size_t)split * p.P + row0 + col0) * p.Mtot + m * 128 + row;
-#pragma unroll
-      for (int n = 0; n < CPT; ++n)
-        if (col0 + n < ncount) o[(size_t)n * p.Mtot] = r[n];
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
-}
-
-template <int BN>
-static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& gp,
-                       int max_tiles, cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    D3_CUDA_TRY(cudaFuncSetAttribute(moe_gemm_kernel<BN>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM),
-                "gemm smem attribute");
-    attr_set[dev] = true;
-  }
-  int grid = num_sms();
-  if (max_tiles < grid) grid = max_tiles;
-  if (grid < 1) grid = 1;
-  D3_CUDA_TRY(launch_k(moe_gemm_kernel<BN>, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st,
-                       pdl_enabled(), tw, tx, gp),
-              "moe_gemm_kernel launch");
-  return D3_OK;
-}
+// (tile engine in gemm_sm100.cuh)
 
 }  // namespace d3
 
@@ -714,8 +500,8 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   g1.rows_per_expert = 2 * I; g1.mblocks = 2 * I / 128; g1.kblocks = H / 128;
   g1.xscale = xs; g1.K = H; g1.out = ws1; g1.P = P; g1.Mtot = 2 * I; g1.kbps = pl.kbps1;
   g1.err = err_word;
-  rc = pl.BN == 16 ? launch_gemm<16>(tw1, tx1, g1, pl.maxt1, st)
-                   : launch_gemm<64>(tw1, tx1, g1, pl.maxt1, st);
+  rc = pl.BN == 16 ? launch_gemm<16, 2>(tw1, tx1, g1, pl.maxt1, st)
+                   : launch_gemm<64, 2>(tw1, tx1, g1, pl.maxt1, st);
   if (rc) return rc;
 
   uint8_t* hq = (uint8_t*)(ws + pl.o_hq);
@@ -735,8 +521,8 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   g2.rows_per_expert = H; g2.mblocks = H / 128; g2.kblocks = I / 128;
   g2.xscale = hs; g2.K = I; g2.out = ws2; g2.P = P; g2.Mtot = H; g2.kbps = pl.kbps2;
   g2.err = err_word;
-  rc = pl.BN == 16 ? launch_gemm<16>(tw2, tx2, g2, pl.maxt2, st)
-                   : launch_gemm<64>(tw2, tx2, g2, pl.maxt2, st);
+  rc = pl.BN == 16 ? launch_gemm<16, 2>(tw2, tx2, g2, pl.maxt2, st)
+                   : launch_gemm<64, 2>(tw2, tx2, g2, pl.maxt2, st);
   if (rc) return rc;
   {
     const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
