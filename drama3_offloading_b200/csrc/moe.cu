@@ -154,8 +154,10 @@ struct RouteParams {
   uint8_t* xq; float* xs;
 };
 
-__device__ void quant_x_block(const __nv_bfloat16* __restrict__ x, int pair, int topk, int H,
-                              int row, int kb, uint8_t* __restrict__ xq, float* __restrict__ xs);
+__device__ __forceinline__ void load_x_block(const __nv_bfloat16* __restrict__ x, int pair,
+                                             int topk, int H, int kb, float (&v)[4]);
+__device__ __forceinline__ void store_x_block(const float (&v)[4], int H, int row, int kb,
+                                              uint8_t* __restrict__ xq, float* __restrict__ xs);
 
 __device__ __forceinline__ int load_pair_id(const void* ids, int bytes, int i, int n) {
   long long v = bytes == 8 ? static_cast<const long long*>(ids)[i]
@@ -253,10 +255,29 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   for (int i = warp_tot[31] + tid; i < p.P; i += blockDim.x) p.sorted[i] = -1;
   __syncthreads();
   if (p.fuse_quant) {
+    // only the valid rows: the GEMM never uses a column past an expert's
+    // pair count, so padding rows need no planes; four blocks per warp with
+    // their loads issued together
     const int nkb = p.H / 128;
-    for (int w = warp; w < p.Ppad * nkb; w += 32) {
-      const int row = w / nkb, kb = w - row * nkb;
-      quant_x_block(p.x, row < p.P ? p.sorted[row] : -1, p.topk, p.H, row, kb, p.xq, p.xs);
+    const int nblk = warp_tot[31] * nkb;
+    for (int w0 = warp * 4; w0 < nblk; w0 += 32 * 4) {
+      float v[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int w = w0 + u;
+        if (w < nblk) {
+          const int row = w / nkb, kb = w - row * nkb;
+          load_x_block(p.x, p.sorted[row], p.topk, p.H, kb, v[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int w = w0 + u;
+        if (w < nblk) {
+          const int row = w / nkb, kb = w - row * nkb;
+          store_x_block(v[u], p.H, row, kb, p.xq, p.xs);
+        }
+      }
     }
   }
   // tile lists: for expert e, N tile j, split s, M tile m
@@ -309,47 +330,48 @@ __device__ __forceinline__ float quant_block(const float (&v)[4], uint32_t& hi4,
   return amax > 0.f ? amax / 448.f : 0.f;
 }
 
-// One warp: the 128-wide K block kb of sorted row `row` (pair `pair`, or
-// zeros when pair < 0) -> hi/lo planes and scale.
-__device__ void quant_x_block(const __nv_bfloat16* __restrict__ x, int pair, int topk, int H,
-                              int row, int kb, uint8_t* __restrict__ xq, float* __restrict__ xs) {
+// One warp, one 128-wide K block of a pair's token row: 4 values per lane.
+__device__ __forceinline__ void load_x_block(const __nv_bfloat16* __restrict__ x, int pair,
+                                             int topk, int H, int kb, float (&v)[4]) {
   const int lane = threadIdx.x & 31;
-  const int nkb = H / 128;
-  float v[4];
-  uint8_t* qrow = xq + (size_t)row * 2 * H;
-  if (pair < 0) {  // rows past the valid pairs (skipped ids)
-    v[0] = v[1] = v[2] = v[3] = 0.f;
-  } else {
-    const int t = pair / topk;
-    const __nv_bfloat16* src = x + (size_t)t * H + kb * 128 + lane * 4;
-    const uint2 raw = *reinterpret_cast<const uint2*>(src);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  const int t = pair / topk;
+  const uint2 raw = *reinterpret_cast<const uint2*>(x + (size_t)t * H + kb * 128 + lane * 4);
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = __bfloat162float(b[q]);
-  }
-  uint32_t hi4, lo4;
-  const float s = quant_block(v, hi4, lo4);
-  *reinterpret_cast<uint32_t*>(qrow + kb * 128 + lane * 4) = hi4;
-  *reinterpret_cast<uint32_t*>(qrow + H + kb * 128 + lane * 4) = lo4;
-  if (lane == 0) xs[(size_t)row * nkb + kb] = s;
+  for (int q = 0; q < 4; ++q) v[q] = __bfloat162float(b[q]);
 }
 
-// One warp per (sorted row, K block): x row of the pair's token -> planes.
-// Rows past the valid pairs (and up to Ppad) become zeros.
+// ... -> the hi/lo planes and the block scale of sorted row `row`.
+__device__ __forceinline__ void store_x_block(const float (&v)[4], int H, int row, int kb,
+                                              uint8_t* __restrict__ xq, float* __restrict__ xs) {
+  const int lane = threadIdx.x & 31;
+  uint32_t hi4, lo4;
+  const float s = quant_block(v, hi4, lo4);
+  uint8_t* qrow = xq + (size_t)row * 2 * H;
+  *reinterpret_cast<uint32_t*>(qrow + kb * 128 + lane * 4) = hi4;
+  *reinterpret_cast<uint32_t*>(qrow + H + kb * 128 + lane * 4) = lo4;
+  if (lane == 0) xs[(size_t)row * (H / 128) + kb] = s;
+}
+
+// One warp per (sorted row, K block) of the valid rows.  Rows past the valid
+// pair count are never read as an in-range column by the GEMM, so they are
+// left unwritten.
 __global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted,
-                               int P, int Ppad, int topk, int H, uint8_t* __restrict__ xq,
-                               float* __restrict__ xs) {
+                               const int* __restrict__ nvalid_ptr, int topk, int H,
+                               uint8_t* __restrict__ xq, float* __restrict__ xs) {
   pdl_trigger();
   pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nkb = H / 128;
-  if (gw >= Ppad * nkb) return;
+  if (gw >= *nvalid_ptr * nkb) return;
   const int row = gw / nkb, kb = gw - row * nkb;
-  quant_x_block(x, row < P ? sorted[row] : -1, topk, H, row, kb, xq, xs);
+  float v[4];
+  load_x_block(x, sorted[row], topk, H, kb, v);
+  store_x_block(v, H, row, kb, xq, xs);
 }
 
-// One warp per (sorted row, K block of I): sum splits, SwiGLU, quantise.
-// Rows at or past the valid pair count (device word) become zeros.
+// One warp per (sorted row, K block of I) of the valid rows: sum splits,
+// SwiGLU, quantise.
 __global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int Ppad,
                            const int* __restrict__ nvalid_ptr, int I, uint8_t* __restrict__ hq,
                            float* __restrict__ hs) {
@@ -357,11 +379,11 @@ __global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int 
   pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int nkb = I / 128;
-  if (gw >= Ppad * nkb) return;
+  if (gw >= *nvalid_ptr * nkb) return;
   const int row = gw / nkb, kb = gw - row * nkb;
-  const int nsplit = row < *nvalid_ptr ? split : 0;
+  (void)Ppad;
   float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < nsplit; ++s) {
+  for (int s = 0; s < split; ++s) {
     const float* r = ws1 + ((size_t)s * P + row) * 2 * I + kb * 128 + lane * 4;
     const float4 a = *reinterpret_cast<const float4*>(r);
     const float4 b = *reinterpret_cast<const float4*>(r + I);
@@ -487,8 +509,8 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   if (!rp.fuse_quant) {
     const long warps = (long)pl.Ppad * (H / 128);
     D3_CUDA_TRY(launch_k(quant_x_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
-                         st, pdl, static_cast<const __nv_bfloat16*>(x), (const int*)rp.sorted, P,
-                         pl.Ppad, topk, H, xq, xs),
+                         st, pdl, static_cast<const __nv_bfloat16*>(x), (const int*)rp.sorted,
+                         (const int*)(rp.ntiles + 2), topk, H, xq, xs),
                 "quant_x_kernel launch");
   }
   CUtensorMap tw1, tx1, tw2, tx2;
