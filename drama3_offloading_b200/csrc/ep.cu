@@ -150,7 +150,8 @@ int d3_ep_dispatch_pack(const void* x, const int32_t* ids, int32_t T, int32_t to
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = pdl_enabled();
   EpPackParams p{ids, T, topk, n_ranks, experts_per_rank, cap, send_eid, src_slot, overflow};
-  D3_CUDA_TRY(launch_k(ep_plan_kernel, dim3(1), dim3(256), 0, st, pdl, p), "ep_plan_kernel");
+  // first launch of the call: an ordinary stream dependent of the caller's work
+  D3_CUDA_TRY(launch_k(ep_plan_kernel, dim3(1), dim3(256), 0, st, false, p), "ep_plan_kernel");
   D3_CUDA_TRY(launch_k(ep_copy_kernel, dim3((unsigned)(T * topk)), dim3(128), 0, st, pdl,
                        static_cast<const __nv_bfloat16*>(x), (const int32_t*)src_slot, topk, H,
                        static_cast<__nv_bfloat16*>(send_x)),
@@ -165,7 +166,7 @@ int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
   D3_CHECK_ARG(T >= 1 && topk >= 1 && H >= 4 && H % 4 == 0, "bad shape");
   if (!aligned16(ret) || !aligned16(out)) return fail(D3_ERR_MISALIGNED, "ret/out not aligned");
   const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
-  D3_CUDA_TRY(launch_k(ep_combine_kernel, grid, dim3(128), 0, (cudaStream_t)stream, pdl_enabled(),
+  D3_CUDA_TRY(launch_k(ep_combine_kernel, grid, dim3(128), 0, (cudaStream_t)stream, false,
                        static_cast<const __nv_bfloat16*>(ret), src_slot, weights, weights_f32, T,
                        topk, H, accumulate ? 1 : 0, static_cast<__nv_bfloat16*>(out)),
               "ep_combine_kernel");

@@ -668,7 +668,7 @@ int d3_prefill_plan(const void* ids, int32_t ids_bytes, int32_t n_pairs, int32_t
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "prefill plan smem attribute");
   D3_CUDA_TRY(launch_k(prefill_plan_kernel, dim3(1), dim3(1024), smem, (cudaStream_t)stream,
-                       pdl_enabled(), ids, ids_bytes, n_pairs, num_experts, expert_list,
+                       false, ids, ids_bytes, n_pairs, num_experts, expert_list,
                        n_distinct, remap, local_ids),
               "prefill_plan_kernel launch");
   return D3_OK;
@@ -707,7 +707,7 @@ int d3_gather_experts(const d3_layer_cache* L, const int32_t* expert_list,
   gp.counters = counters;
   const int ctas = fetch_ctas > 0 ? fetch_ctas : num_sms();
   D3_CUDA_TRY(launch_k(gather_kernel, dim3((unsigned)ctas), dim3(kFetchThreads), 0,
-                       (cudaStream_t)stream, pdl_enabled(), gp),
+                       (cudaStream_t)stream, false, gp),
               "gather_kernel launch");
   return D3_OK;
 }

@@ -503,7 +503,10 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
     D3_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)rsmem),
                 "route smem attribute");
-  D3_CUDA_TRY(launch_k(route_kernel, dim3(1), dim3(1024), rsmem, st, pdl, rp),
+  // The first launch of a call is an ordinary stream dependent: whatever the
+  // caller queued before it (copies, foreign kernels) must complete first;
+  // only the launches inside this call are chained programmatically.
+  D3_CUDA_TRY(launch_k(route_kernel, dim3(1), dim3(1024), rsmem, st, false, rp),
               "route_kernel launch");
   int rc = D3_OK;
   if (!rp.fuse_quant) {

@@ -202,3 +202,22 @@ def test_moe_forward_accumulate_into_input():
     moe.check_errors(DEV)
     want = xd.float() + plain.float()
     assert rel_err(h, want) < 1e-2
+
+
+@pytest.mark.parametrize("E,T,k", [(8, 512, 8), (64, 16, 8), (68, 1, 8)])
+def test_moe_forward_deterministic_with_fresh_inputs(E, T, k):
+    """Repeated calls, each right after fresh host->device copies of its inputs,
+    give bit-identical results (no launch of a call may start before the
+    caller's preceding stream work)."""
+    ex, x, ids, w = _rand_case(E, T, k, 77)
+    outs = []
+    for _ in range(3):
+        xd, idd, wd = x.to(DEV), ids.to(DEV), w.to(DEV)
+        out = moe.fp8_moe_forward(xd, idd, wd, ex.w13_weight, ex.w13_scale_inv, ex.w2_weight,
+                                  ex.w2_scale_inv)
+        outs.append(out.clone())
+        del xd, idd, wd
+    torch.cuda.synchronize()
+    moe.check_errors(DEV)
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    assert torch.isfinite(outs[0].float()).all()
