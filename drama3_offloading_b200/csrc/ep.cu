@@ -78,9 +78,10 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(EpPackParams p) {
 }
 
 // One CTA per pair: copy x[t] into its send row.
-__global__ void __launch_bounds__(128) ep_copy_kernel(const __nv_bfloat16* __restrict__ x,
-                                                      const int32_t* __restrict__ src_slot,
-                                                      int topk, int H,
+// src_slot is written by the overlapping plan launch: no __restrict__ (no
+// non-coherent reads of it).
+__global__ void __launch_bounds__(128) ep_copy_kernel(const __nv_bfloat16* x,
+                                                      const int32_t* src_slot, int topk, int H,
                                                       __nv_bfloat16* __restrict__ send_x) {
   pdl_trigger();
   pdl_wait();

@@ -215,11 +215,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
       epi_bar_sync(NEPI);  // every epilogue thread is done with the previous tile's scales
       if (ep == 0) s_tile_abort = s_abort;
       const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
+      // Coherent (L2) loads, never the non-coherent read-only path: under
+      // programmatic launch this kernel's lifetime overlaps the kernels that
+      // write these scales (for a reused workspace, a line cached by an
+      // earlier call could otherwise be served stale).
       for (int i = ep; i < nkb * BN; i += NEPI) {
         const int j = i / BN, n = i - j * BN;
         s_scale[i] = n < ncount
-                         ? __ldg(ws + kb0 + j) *
-                               __ldg(p.xscale + (size_t)(row0 + n) * p.kblocks + kb0 + j)
+                         ? __ldcg(ws + kb0 + j) *
+                               __ldcg(p.xscale + (size_t)(row0 + n) * p.kblocks + kb0 + j)
                          : 0.f;
       }
       epi_bar_sync(NEPI);

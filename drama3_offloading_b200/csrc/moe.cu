@@ -356,9 +356,12 @@ __device__ __forceinline__ void store_x_block(const float (&v)[4], int H, int ro
 // One warp per (sorted row, K block) of the valid rows.  Rows past the valid
 // pair count are never read as an in-range column by the GEMM, so they are
 // left unwritten.
-__global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted,
-                               const int* __restrict__ nvalid_ptr, int topk, int H,
-                               uint8_t* __restrict__ xq, float* __restrict__ xs) {
+// (Pointers to data an overlapping launch writes carry no __restrict__, so no
+// read of them takes the non-coherent read-only path; the same in the
+// kernels below.)
+__global__ void quant_x_kernel(const __nv_bfloat16* x, const int* sorted, const int* nvalid_ptr,
+                               int topk, int H, uint8_t* __restrict__ xq,
+                               float* __restrict__ xs) {
   pdl_trigger();
   pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -372,9 +375,8 @@ __global__ void quant_x_kernel(const __nv_bfloat16* __restrict__ x, const int* _
 
 // One warp per (sorted row, K block of I) of the valid rows: sum splits,
 // SwiGLU, quantise.
-__global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int Ppad,
-                           const int* __restrict__ nvalid_ptr, int I, uint8_t* __restrict__ hq,
-                           float* __restrict__ hs) {
+__global__ void act_kernel(const float* ws1, int split, int P, int Ppad, const int* nvalid_ptr,
+                           int I, uint8_t* __restrict__ hq, float* __restrict__ hs) {
   pdl_trigger();
   pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -402,10 +404,9 @@ __global__ void act_kernel(const float* __restrict__ ws1, int split, int P, int 
 }
 
 // out[t, j] = bf16( [out[t,j] +] sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
-__global__ void combine_kernel(const float* __restrict__ ws2, int split, int P, int H,
-                               const int* __restrict__ inv, const void* __restrict__ weights,
-                               int weights_f32, int T, int topk, int accumulate,
-                               __nv_bfloat16* __restrict__ out) {
+__global__ void combine_kernel(const float* ws2, int split, int P, int H, const int* inv,
+                               const void* weights, int weights_f32, int T, int topk,
+                               int accumulate, __nv_bfloat16* out) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.y;
