@@ -84,6 +84,7 @@ static int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_
 
 constexpr int kMaxExperts = 8192;
 constexpr int kMaxPairs = 65536;
+constexpr int kFusedQuantMaxPairs = 256;   // route quantises in-launch up to this many pairs
 
 struct Plan {
   int P;        // routed pairs = T * topk
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   int* cursor = sm;            // [n]
   int* tcount = sm + p.n;      // [n] N tiles per expert, then its prefix
   __shared__ int warp_tot[32];
+  __shared__ int s_sorted[kFusedQuantMaxPairs];  // row -> pair, for the fused quantisation
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_trigger();
   pdl_wait();
@@ -246,6 +248,7 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
       if (e >= 0) {
         const int pos = base + rank;
         p.sorted[pos] = i;
+        if (p.fuse_quant) s_sorted[pos] = i;  // fuse_quant implies P <= kFusedQuantMaxPairs
         p.inv[i] = pos;
       }
       __syncwarp();
@@ -267,7 +270,7 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
         const int w = w0 + u;
         if (w < nblk) {
           const int row = w / nkb, kb = w - row * nkb;
-          load_x_block(p.x, p.sorted[row], p.topk, p.H, kb, v[u]);
+          load_x_block(p.x, s_sorted[row], p.topk, p.H, kb, v[u]);
         }
       }
 #pragma unroll
@@ -495,7 +498,8 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
   float* xs = (float*)(ws + pl.o_xs);
   // small batches quantise inside the route launch (one CTA, 32 warps)
-  rp.fuse_quant = (long)pl.Ppad * (H / 128) <= 32L * 32 ? 1 : 0;
+  rp.fuse_quant =
+      ((long)pl.Ppad * (H / 128) <= 32L * 32 && P <= kFusedQuantMaxPairs) ? 1 : 0;
   rp.x = static_cast<const __nv_bfloat16*>(x);
   rp.topk = topk; rp.H = H; rp.Ppad = pl.Ppad; rp.xq = xq; rp.xs = xs;
   const bool pdl = pdl_enabled();

@@ -87,31 +87,41 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
         const int c = c0 + 32 * u;
         if (c >= vec_per_row) break;
         const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
-        double wd[8];
+        float wf[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) wd[q] = (double)__bfloat162float(wb[q]);
+        for (int q = 0; q < 8; ++q) wf[q] = __bfloat162float(wb[q]);
 #pragma unroll
         for (int t = 0; t < kRouterTokensPerCta; ++t) {
           if (t < nt) {
             const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
             const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              acc[t] = fma((double)__bfloat162float(xb[q]), wd[q], acc[t]);
+            for (int q = 0; q < 8; ++q) {
+              // a bf16 x bf16 product has 16 significant bits: exact in fp32
+              // unless it leaves fp32's normal range, where fp64 takes over
+              const float xf = __bfloat162float(xb[q]);
+              const float pr = xf * wf[q];
+              const float ap = fabsf(pr);
+              acc[t] += (ap >= 0x1p-100f && ap <= 0x1p100f)
+                            ? (double)pr
+                            : (double)xf * (double)wf[q];
+            }
           }
         }
       }
     }
 #pragma unroll
     for (int t = 0; t < kRouterTokensPerCta; ++t) {
-      double v = acc[t];
+      if (t < nt) {
+        double v = acc[t];
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0 && t < nt) p.logits[(size_t)(t0 + t) * p.E + e] = exact_bf16_of(v);
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) p.logits[(size_t)(t0 + t) * p.E + e] = exact_bf16_of(v);
+      }
     }
+    if (lane == 0) __threadfence();  // the logit stores before this CTA's arrival
   }
   // last CTA of this token tile does the selection
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned prev = atomicAdd(p.arrivals + blockIdx.y, 1u);
