@@ -87,25 +87,17 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
         const int c = c0 + 32 * u;
         if (c >= vec_per_row) break;
         const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
-        float wf[8];
+        double wd[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) wf[q] = __bfloat162float(wb[q]);
+        for (int q = 0; q < 8; ++q) wd[q] = (double)__bfloat162float(wb[q]);
 #pragma unroll
         for (int t = 0; t < kRouterTokensPerCta; ++t) {
           if (t < nt) {
             const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
             const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              // a bf16 x bf16 product has 16 significant bits: exact in fp32
-              // unless it leaves fp32's normal range, where fp64 takes over
-              const float xf = __bfloat162float(xb[q]);
-              const float pr = xf * wf[q];
-              const float ap = fabsf(pr);
-              acc[t] += (ap >= 0x1p-100f && ap <= 0x1p100f)
-                            ? (double)pr
-                            : (double)xf * (double)wf[q];
-            }
+            for (int q = 0; q < 8; ++q)
+              acc[t] = fma((double)__bfloat162float(xb[q]), wd[q], acc[t]);
           }
         }
       }
