@@ -1,7 +1,7 @@
 """Benchmark of the routed-MoE expert-offload hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|fetch]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload decode|fetch|prefill|ep|layer] [--impl ours|reference]
 
 Workloads:
 
@@ -14,6 +14,12 @@ Workloads:
   against the measured pinned copy-engine peak is reported beside it.
 * ``fetch`` -- configs[1]: the expert-fetch microbenchmark (40 x 256 experts
   pinned, 2048 slots in total, graph-captured allocator + fetch per layer).
+* ``prefill`` -- configs[3]: a 2048-token chunk through 40 offloaded layers
+  (union gather + token-permuted FP8 grouped GEMM).
+* ``ep`` -- configs[4]: resident expert-parallel decode, batch 64, 256 experts
+  sharded over N GPUs, NCCL all-to-all dispatch/combine.
+* ``layer`` -- configs[0]: one MoE layer over 16 tokens with 256 resident
+  experts, the CPU restatement timed beside it.
 
 Inputs are far larger than L2 (30 GiB host store, 6.9 GiB dense weights, 8 GiB
 cache).  Multi-GPU runs are replicas (each rank its own store, cache and host
@@ -44,7 +50,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "fetch", "ep", "prefill"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "fetch", "ep", "prefill", "layer"),
+                    default="decode")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--global-batch", type=int, default=64, help="ep workload: decode streams")
     ap.add_argument("--layers", type=int, default=40)
@@ -427,6 +434,149 @@ def run_prefill(args, rank, world, local):
     }
 
 
+# ---------------------------------------------------------------- layer
+
+METRIC_LAYER = "single MoE layer tok/s (T=16, 256 resident FP8 experts, top-8)"
+
+
+def run_layer(args, rank, world, local):
+    """one MoE layer -- router + FP8 expert GEMMs -- over 16 decode
+    tokens (hidden 2048, 256 experts resident in HBM, intermediate 512,
+    N(0,0.02) weights quantised per 128x128 block, router N(0,0.02), x N(0,1),
+    seed 0).  One step = one layer call, graph-replayed; each step routes a
+    different 16-token batch (64 prepared batches), so the ~100 distinct
+    experts a step reads (~320 MB) come from HBM, not L2.  Parity against the
+    oracle (ids bit-exact, hidden rel <= 1e-2) is checked on batch 0; the CPU
+    restatement (oracle router + dequantise-then-matmul) is timed on the host
+    cores beside it."""
+    from drama3_offloading_b200 import benchutil, moe, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T, E, NB = 16, 256, 64
+    ex = synth.make_experts(E, seed=0, device="cuda", chunk=32)
+    g = torch.Generator().manual_seed(0)
+    gate_c = (torch.randn(E, 2048, generator=g) * 0.02).to(torch.bfloat16)
+    xs_c = [torch.randn(T, 2048, generator=g).to(torch.bfloat16) for _ in range(NB)]
+    gate = gate_c.to(dev)
+    xs = torch.stack(xs_c).to(dev)                       # [NB, T, H]
+    ids = torch.empty(T, 8, dtype=torch.int32, device=dev)
+    wts = torch.empty(T, 8, dtype=torch.float32, device=dev)
+    out = torch.empty(T, 2048, dtype=torch.bfloat16, device=dev)
+    sel = torch.zeros(1, dtype=torch.int64, device=dev)
+    xcur = torch.empty(T, 2048, dtype=torch.bfloat16, device=dev)
+
+    def layer(x):
+        moe.router_topk(x, gate, 8, out_ids=ids, out_w=wts)
+        moe.fp8_moe_forward(x, ids, wts, ex.w13_weight, ex.w13_scale_inv, ex.w2_weight,
+                            ex.w2_scale_inv, out=out)
+
+    def step():
+        xcur.copy_(xs.index_select(0, sel)[0])
+        sel.add_(1).remainder_(NB)
+        layer(xcur)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with benchutil.ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("timed")
+        a.record()
+        for _ in range(args.steps):
+            gr.replay()
+        b.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.steps
+    # distinct experts per batch -> algorithmic HBM bytes of the expert GEMMs
+    distinct = []
+    for i in range(NB):
+        moe.router_topk(xs[i], gate, 8, out_ids=ids, out_w=wts)
+        distinct.append(int(torch.unique(ids).numel()))
+    alg_bytes = float(np.mean(distinct)) * EXPERT_BYTES + E * 2048 * 2
+    # the moe call alone, for the roofline of the expert GEMMs
+    evs = []
+    for i in range(NB):
+        moe.router_topk(xs[i], gate, 8, out_ids=ids, out_w=wts)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        moe.fp8_moe_forward(xs[i], ids, wts, ex.w13_weight, ex.w13_scale_inv, ex.w2_weight,
+                            ex.w2_scale_inv, out=out)
+        e1.record()
+        evs.append((e0, e1, distinct[i]))
+    torch.cuda.synchronize(dev)
+    moe_ms = float(np.mean([x.elapsed_time(y) for x, y, _ in evs[4:]]))
+    moe_gbs = float(np.mean([d * EXPERT_BYTES / (x.elapsed_time(y) * 1e-3) / 1e9
+                             for x, y, d in evs[4:]]))
+    # e2e through the public API with host buffers: x pinned host -> device,
+    # router + experts, out -> pinned host, every step
+    hx = xs_c[0].pin_memory()
+    ho = torch.empty(T, 2048, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(T, 2048, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        xd.copy_(hx, non_blocking=True); layer(xd); ho.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        xd.copy_(hx, non_blocking=True)
+        layer(xd)
+        ho.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    # parity on batch 0 and the CPU restatement beside it
+    import oracle
+    layer(xs[0])
+    torch.cuda.synchronize(dev)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu_ex = ex.to("cpu")
+    t0 = time.perf_counter()
+    rid, rw, _, _ = oracle.router_topk(xs_c[0], gate_c, 8)
+    ref = oracle.moe_forward(xs_c[0], rid, rw, cpu_ex.w13_weight, cpu_ex.w13_scale_inv,
+                             cpu_ex.w2_weight, cpu_ex.w2_scale_inv)
+    cpu_s = time.perf_counter() - t0
+    ids_exact = bool(np.array_equal(ids.cpu().numpy(), rid.numpy()))
+    rel = float((out.float().cpu() - ref).abs().max() / ref.abs().max())
+    peak = measured_peaks()
+    return {
+        "metric": METRIC_LAYER, "value": T / (ms * 1e-3), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8 weights x (bf16-class hi/lo fp8 activations)",
+        "data": "synthetic (configs[0]: N(0,0.02) FP8 experts, bf16 router, N(0,1) tokens, seed 0)",
+        "config": {"workload": "single-moe-layer", "tokens": T, "experts": E, "hidden": 2048,
+                   "intermediate": 512, "topk": 8, "parallelism": "single",
+                   "l2": "inputs > L2 (805 MB of experts, a new 16-token batch each step)"},
+        "layer_us": ms * 1e3, "moe_us": moe_ms * 1e3,
+        "distinct_experts_per_step": float(np.mean(distinct)),
+        "roofline": {"bound": "hbm", "kernel": "d3_moe_fp8_forward (expert GEMMs)",
+                     "achieved": moe_gbs, "peak": peak["hbm_gbs"], "unit": "GB/s",
+                     "frac": moe_gbs / peak["hbm_gbs"], "traffic": None,
+                     "bytes": "distinct experts x 3,146,496 B",
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak['source']})"},
+        "layer_roofline_frac": alg_bytes / (peak["hbm_gbs"] * 1e9) / (ms * 1e-3),
+        "parity": {"ids_bit_exact": ids_exact, "rel_err": rel, "tolerance": 1e-2},
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s",
+                "h2d_bytes_per_step": T * 2048 * 2, "d2h_bytes_per_step": T * 2048 * 2},
+        "cpu_baseline": {"value": T / cpu_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": "batch 0 (16 tokens): oracle router + dequantise-then-matmul "
+                                   "fp32 experts, torch on all host threads"},
+        "clocks": clk.summary(), "gpu_launches": args.steps * 7,
+    }
+
+
 # ---------------------------------------------------------------- ep (configs[4])
 
 def run_ep(args, rank, world, local):
@@ -558,8 +708,9 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.workload in ("ep", "prefill"):
-        r = (run_ep if args.workload == "ep" else run_prefill)(args, rank, world, local)
+    if args.workload in ("ep", "prefill", "layer"):
+        run = {"ep": run_ep, "prefill": run_prefill, "layer": run_layer}[args.workload]
+        r = run(args, rank, world, local)
         if rank == 0:
             print(json.dumps(r), flush=True)
         if world > 1:
@@ -601,7 +752,7 @@ def main():
                 "metric": METRIC_DECODE, "value": r["value"], "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "fp8 weights x (bf16-class hi/lo fp8 activations), bf16 dense",
+                "dtype": "fp8 weights x bf16 activations (fp32 accumulate), bf16 dense",
                 "data": "synthetic (random-init Drama-3 shapes, seeded Zipf(1.1) routing trace)",
                 "config": {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
                            "hidden": 2048, "experts": 256, "topk": 8, "cache_gib": args.cache_gib,

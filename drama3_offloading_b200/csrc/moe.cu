@@ -31,6 +31,7 @@
 // once per N tile; K-splits spread a small batch's few experts over all SMs.
 #include "d3_common.cuh"
 #include "gemm_sm100.cuh"
+#include "moe_gemv.cuh"
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -445,6 +446,74 @@ __global__ void combine_kernel(const float* ws2, int split, int P, int H, const 
 // ---------------------------------------------------------------- 3/5. GEMM
 // (tile engine in gemm_sm100.cuh)
 
+// ---------------------------------------------------------------- small batch
+// (GEMV kernels in moe_gemv.cuh)
+
+// measured on B200 (8 distinct experts per token, weights from HBM): the GEMV
+// path takes 13.9 / 23.8 / 40.0 us at 8 / 16 / 32 pairs against 30.4 / 42.2 /
+// 60.6 us for the tensor-core path
+constexpr int kGemvMaxPairsDefault = 32;
+
+// Pairs up to which the CUDA-core GEMV path runs (D3_GEMV_MAX_PAIRS
+// overrides; 0 sends every batch to the tensor-core path).
+static int gemv_max_pairs() {
+  const char* s = getenv("D3_GEMV_MAX_PAIRS");
+  return s ? atoi(s) : kGemvMaxPairsDefault;
+}
+
+static size_t gemv2_smem(int topk, int I) { return (size_t)topk * (I / 16) * 20 * sizeof(float); }
+
+static bool gemv_supported(int P, int topk, int H, int I) {
+  const int c1 = H / 512, c2 = I / 512;
+  return P <= gemv_max_pairs() && H % 512 == 0 && I % 512 == 0 &&
+         (c1 == 1 || c1 == 2 || c1 == 4 || c1 == 8) && (c2 == 1 || c2 == 2 || c2 == 4) &&
+         gemv2_smem(topk, I) <= 96 * 1024;
+}
+
+template <int C1>
+static cudaError_t launch_gemv13(const GemvParams& gp, int ctas, cudaStream_t st) {
+  return launch_k(moe_gemv13_kernel<C1>, dim3((unsigned)ctas), dim3(kGemvThreads), 0, st, false,
+                  gp);
+}
+
+template <int C2>
+static cudaError_t launch_gemv2(const GemvParams& gp, dim3 grid, int rpw, size_t smem,
+                                cudaStream_t st, bool pdl) {
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        moe_gemv2_kernel<C2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_k(moe_gemv2_kernel<C2>, grid, dim3(kGemvThreads), smem, st, pdl, gp, rpw);
+}
+
+static int run_gemv(const GemvParams& gp, cudaStream_t st) {
+  const int sms = num_sms();
+  const long units1 = (long)gp.T * gp.topk * gp.I;  // one warp each
+  long ctas1 = (units1 + kGemvRowsPerCta - 1) / kGemvRowsPerCta;
+  if (ctas1 > 2L * sms) ctas1 = 2L * sms;  // one resident wave (2 CTAs per SM)
+  cudaError_t e;
+  switch (gp.H / 512) {
+    case 1: e = launch_gemv13<1>(gp, (int)ctas1, st); break;
+    case 2: e = launch_gemv13<2>(gp, (int)ctas1, st); break;
+    case 4: e = launch_gemv13<4>(gp, (int)ctas1, st); break;
+    default: e = launch_gemv13<8>(gp, (int)ctas1, st); break;
+  }
+  D3_CUDA_TRY(e, "moe_gemv13_kernel launch");
+  int rpw = 1;  // output rows per warp: more once the grid would exceed ~4 CTAs per SM
+  while (rpw < 4 && (long)gp.T * gp.H / (kGemvRowsPerCta * rpw) > 4L * sms) rpw *= 2;
+  const dim3 grid2((unsigned)(gp.H / (kGemvRowsPerCta * rpw)), (unsigned)gp.T);
+  const size_t smem = gemv2_smem(gp.topk, gp.I);
+  const bool pdl = pdl_enabled();
+  switch (gp.I / 512) {
+    case 1: e = launch_gemv2<1>(gp, grid2, rpw, smem, st, pdl); break;
+    case 2: e = launch_gemv2<2>(gp, grid2, rpw, smem, st, pdl); break;
+    default: e = launch_gemv2<4>(gp, grid2, rpw, smem, st, pdl); break;
+  }
+  D3_CUDA_TRY(e, "moe_gemv2_kernel launch");
+  return D3_OK;
+}
+
 }  // namespace d3
 
 using namespace d3;
@@ -485,6 +554,22 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = (cudaStream_t)stream;
   const int P = pl.P;
+
+  if (gemv_supported(P, topk, H, I)) {
+    // decode-sized batch: two CUDA-core launches; h lives where gemm1's
+    // partials would (split1 * P * 2I floats >= P * I)
+    GemvParams gp{};
+    gp.x = static_cast<const __nv_bfloat16*>(x);
+    gp.ids = ids; gp.ids_bytes = ids_bytes;
+    gp.weights = weights; gp.weights_f32 = weights_f32 ? 1 : 0;
+    gp.T = T; gp.topk = topk; gp.n = n_experts; gp.H = H; gp.I = I;
+    gp.accumulate = accumulate ? 1 : 0;
+    gp.w13 = static_cast<const uint8_t*>(w13); gp.s13 = s13;
+    gp.w2 = static_cast<const uint8_t*>(w2); gp.s2 = s2;
+    gp.h = (float*)(ws + pl.o_ws1);
+    gp.out = static_cast<__nv_bfloat16*>(out);
+    return run_gemv(gp, st);
+  }
 
   RouteParams rp{};
   rp.ids = ids; rp.ids_bytes = ids_bytes; rp.P = P; rp.n = n_experts;

@@ -1,0 +1,242 @@
+// Small-batch routed-MoE path: the expert GEMMs as matrix-vector products on
+// the CUDA cores, two launches per call.
+//
+// At a decode batch (one token, eight routed pairs) every expert weight byte
+// meets exactly one activation row, so the work is a GEMV over 8 x 3 MiB of
+// fp8 weights: HBM-bound with ~2 FLOP per byte.  The tensor-core path pays a
+// fixed cost that dominates at this size (pair sort, activation planes, TMEM
+// allocation, pipeline fill, split-K partials, a combine pass); this path
+// streams the weights with 16-byte loads and keeps everything else on chip:
+//
+//   gemv13   one warp per (pair, intermediate row j): the gate row j and the
+//            up row I + j of the pair's expert against the token row (held in
+//            registers as fp32), per-128 K-block scales applied to the fp32
+//            partial sums, then h[pair, j] = silu(g) * u  (fp32, workspace).
+//   gemv2    one CTA per (token, 8 output rows): the token's pair rows of h
+//            staged in shared memory; one warp per output row j sums
+//            w[t,k] * s2 * (W2[e_k][j, :] . h[pair_k]) over the token's pairs
+//            and writes out[t, j] (bf16, optionally added to out).  Its first
+//            W2 rows are loaded BEFORE griddepcontrol.wait: they do not depend
+//            on gemv13, so with programmatic launch the down-projection weights
+//            stream in while the gate/up products finish.
+//
+// Activations stay fp32/bf16 (no activation quantisation), so this path is
+// at least as accurate as the tensor-core path; both sum the same products.
+// Ids outside [0, n) skip their pair, as everywhere in this library.
+#pragma once
+
+#include "d3_common.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+namespace d3 {
+
+constexpr int kGemvThreads = 256;                 // 8 warps
+constexpr int kGemvRowsPerCta = kGemvThreads / 32;
+
+struct GemvParams {
+  const __nv_bfloat16* x;   // [T, H]
+  const void* ids;          // [T, topk] int32 or int64
+  int ids_bytes;
+  const void* weights;      // [T, topk] fp32 or bf16
+  int weights_f32;
+  int T, topk, n, H, I, accumulate;
+  const uint8_t* w13;       // [n, 2I, H] e4m3
+  const float* s13;         // [n, 2I/128, H/128]
+  const uint8_t* w2;        // [n, H, I] e4m3
+  const float* s2;          // [n, H/128, I/128]
+  float* h;                 // [T*topk, I] workspace
+  __nv_bfloat16* out;       // [T, H]
+};
+
+__device__ __forceinline__ int gemv_pair_id(const void* ids, int bytes, int i, int n) {
+  const long long v = bytes == 8 ? static_cast<const long long*>(ids)[i]
+                                 : (long long)static_cast<const int*>(ids)[i];
+  return (v >= 0 && v < n) ? (int)v : -1;
+}
+
+// sum_q w[q] * v[q] over one 16-byte chunk of e4m3 weights, two partial sums.
+__device__ __forceinline__ float dot16_e4m3(const uint4 w, const float (&v)[16]) {
+  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(
+        static_cast<__nv_fp8x2_storage_t>(wr[q] & 0xffffu), __NV_E4M3);
+    const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(
+        static_cast<__nv_fp8x2_storage_t>(wr[q] >> 16), __NV_E4M3);
+    const float2 a = __half22float2(__half2(lo));
+    const float2 b = __half22float2(__half2(hi));
+    s0 = fmaf(a.x, v[4 * q + 0], s0);
+    s1 = fmaf(a.y, v[4 * q + 1], s1);
+    s0 = fmaf(b.x, v[4 * q + 2], s0);
+    s1 = fmaf(b.y, v[4 * q + 3], s1);
+  }
+  return s0 + s1;
+}
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4 r, float* v) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[2 * q] = __uint_as_float(w[q] << 16);
+    v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// CPL = 16-byte chunks per lane of a W13 row = H / 512.
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+  const int I = p.I, H = p.H, nkb = H / 128;
+  const long units = (long)p.T * p.topk * I;
+  float xv[CPL][16];
+  int cur_t = -1;
+  for (long u = gw; u < units; u += nw) {
+    const int pair = (int)(u / I), j = (int)(u - (long)pair * I);
+    const int e = gemv_pair_id(p.ids, p.ids_bytes, pair, p.n);
+    if (e < 0) continue;  // warp-uniform: the whole warp works on one unit
+    const uint4* wg = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + j) * H);
+    const uint4* wu = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + I + j) * H);
+    uint4 g[CPL], v[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      g[c] = __ldcg(wg + lane + 32 * c);
+      v[c] = __ldcg(wu + lane + 32 * c);
+    }
+    const int t = pair / p.topk;
+    if (t != cur_t) {
+      cur_t = t;
+      const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * H);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int q = lane + 32 * c;  // K elements [16q, 16q + 16)
+        unpack_bf16x8(xr[2 * q], xv[c]);
+        unpack_bf16x8(xr[2 * q + 1], xv[c] + 8);
+      }
+    }
+    const float* sg = p.s13 + ((size_t)e * (2 * I / 128) + j / 128) * nkb;
+    const float* su = p.s13 + ((size_t)e * (2 * I / 128) + (I + j) / 128) * nkb;
+    float ag = 0.f, au = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const int kb = (lane + 32 * c) >> 3;
+      ag = fmaf(__ldcg(sg + kb), dot16_e4m3(g[c], xv[c]), ag);
+      au = fmaf(__ldcg(su + kb), dot16_e4m3(v[c], xv[c]), au);
+    }
+    ag = warp_sum(ag);
+    au = warp_sum(au);
+    if (lane == 0) p.h[u] = ag / (1.f + expf(-ag)) * au;
+  }
+}
+
+// CPL = 16-byte chunks per lane of a W2 row = I / 512.  Grid (H / 8 / rpw, T);
+// dynamic shared memory: topk rows of h, each 16-float chunk padded to 20
+// floats (conflict-free 16-byte reads: lane l's chunk starts at bank 20 l).
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, int rpw) {
+  constexpr int kGemvPairGroup = 8 / CPL;  // W2 rows (of pairs) a warp keeps in flight
+  extern __shared__ __align__(16) float s_h[];   // [topk][I / 16][20]
+  __shared__ float s_w[64];
+  __shared__ int s_e[64];
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int I = p.I, H = p.H, topk = p.topk, nkbI = I / 128;
+  const int t = blockIdx.y;
+  const int row_stride = I / 16 * 20;
+  const int j_first = (blockIdx.x * rpw) * kGemvRowsPerCta + warp;
+  // ids were written before the gate/up launch started: safe to read early
+  int my_e = -1;
+  if (lane < topk) my_e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + lane, p.n);
+  uint4 w0[kGemvPairGroup][CPL];
+#pragma unroll
+  for (int q = 0; q < kGemvPairGroup; ++q) {
+    const int e = __shfl_sync(0xffffffffu, my_e, q);
+    if (q < topk && e >= 0 && j_first < H) {
+      const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
+    }
+  }
+  pdl_wait();
+  // stage the token's pair rows of h (written by the gate/up launch)
+  for (int i = threadIdx.x; i < topk * (I / 4); i += blockDim.x) {
+    const int k = i / (I / 4), f4 = i - k * (I / 4);
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)(t * topk + k) * I) + f4);
+    *reinterpret_cast<float4*>(s_h + k * row_stride + (f4 >> 2) * 20 + (f4 & 3) * 4) = v;
+  }
+  if (threadIdx.x < topk) {
+    const int i = t * topk + threadIdx.x;
+    s_e[threadIdx.x] = gemv_pair_id(p.ids, p.ids_bytes, i, p.n);
+    s_w[threadIdx.x] = p.weights_f32 ? static_cast<const float*>(p.weights)[i]
+                                     : __bfloat162float(
+                                           static_cast<const __nv_bfloat16*>(p.weights)[i]);
+  }
+  __syncthreads();
+  for (int r = 0; r < rpw; ++r) {
+    const int j = j_first + r * kGemvRowsPerCta;
+    if (j >= H) break;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < topk; k0 += kGemvPairGroup) {
+      uint4 w[kGemvPairGroup][CPL];
+      if (r == 0 && k0 == 0) {
+#pragma unroll
+        for (int q = 0; q < kGemvPairGroup; ++q)
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) w[q][c] = w0[q][c];
+      } else {
+#pragma unroll
+        for (int q = 0; q < kGemvPairGroup; ++q) {
+          const int k = k0 + q;
+          const int e = k < topk ? s_e[k] : -1;
+          if (e >= 0) {
+            const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j) * I);
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) w[q][c] = __ldcg(wr + lane + 32 * c);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kGemvPairGroup; ++q) {
+        const int k = k0 + q;
+        const int e = k < topk ? s_e[k] : -1;
+        if (e < 0) continue;
+        const float* sr = p.s2 + ((size_t)e * (H / 128) + j / 128) * nkbI;
+        float part = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int ch = lane + 32 * c;
+          const float* hp = s_h + k * row_stride + ch * 20;
+          float hv[16];
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            const float4 a = *reinterpret_cast<const float4*>(hp + 4 * f);
+            hv[4 * f] = a.x; hv[4 * f + 1] = a.y; hv[4 * f + 2] = a.z; hv[4 * f + 3] = a.w;
+          }
+          part = fmaf(__ldcg(sr + (ch >> 3)), dot16_e4m3(w[q][c], hv), part);
+        }
+        acc = fmaf(s_w[k], part, acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      __nv_bfloat16* o = p.out + (size_t)t * H + j;
+      if (p.accumulate) acc += __bfloat162float(*o);
+      *o = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+}  // namespace d3

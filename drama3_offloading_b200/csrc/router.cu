@@ -10,12 +10,19 @@
 // both round-to-nearest-even.  Any other accumulation order only changes the
 // fp64 sum's last bits, so every correct implementation agrees on the ids.
 //
-// Kernel shape: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one
-// expert per warp over a tile of 8 tokens staged in shared memory (each gate
-// row is read once per token tile).  The last CTA of a token tile to finish
-// (a global arrival counter, reset by that CTA for the next launch or graph
-// replay) selects the top-k of its tokens: one warp per token, 8 logits per
-// lane for E = 256, k rounds of a warp arg-max.
+// Two kernels share the arithmetic and the selection:
+// * T <= 2 (decode): one thread-block cluster of 8 CTAs; each CTA computes
+//   E/8 experts' logits and stores them into the leader CTA's shared memory
+//   over distributed shared memory; after one cluster barrier the leader
+//   selects.  No global scratch.
+// * T > 2: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one expert
+//   per warp over a tile of 8 tokens staged in shared memory (each gate row is
+//   read once per token tile).  The last CTA of a token tile to finish (a
+//   global arrival counter, reset by that CTA for the next launch or graph
+//   replay) selects the top-k of its tokens from the workspace logits.
+// Selection: one warp per token, logits 32-strided over the lanes, k rounds of
+// a single warp max-reduction over (order-preserving value code, inverted
+// index) keys, so ties go to the lower index.
 #include "d3_common.cuh"
 
 #include <cuda_bf16.h>
@@ -51,6 +58,198 @@ __device__ __forceinline__ float exact_bf16_of(double s) {
   return __bfloat162float(__float2bfloat16_rn(__double2float_rn(s)));
 }
 
+// Selection key of a logit (a bf16 value held in fp32): the order-preserving
+// 16-bit code of the value above the inverted expert index, so the unsigned
+// maximum is the largest logit, ties to the lower index.  -0 is folded into
+// +0 (they compare equal); 0 is below every real key and marks "taken".
+__device__ __forceinline__ unsigned topk_key(float v, int i) {
+  const unsigned b = __float_as_uint(v + 0.0f) >> 16;
+  const unsigned code = (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+  return (code << 16) | (0xffffu - (unsigned)i);
+}
+
+__device__ __forceinline__ float topk_key_value(unsigned key) {
+  const unsigned code = key >> 16;
+  const unsigned b = (code & 0x8000u) ? (code & 0x7fffu) : (~code & 0xffffu);
+  return __uint_as_float(b << 16);
+}
+
+// Top-k of token t's logits, held by one warp 32-strided (v[j] = logit
+// j*32 + lane, -inf past E; per = ceil(E/32)): fp32 softmax (max, then the
+// per-lane sums in j order combined by a butterfly), k rounds of one warp
+// max-reduction over the selection keys, then the optional renormalisation.
+template <int KPER>
+__device__ __forceinline__ void topk_select(const float (&v)[KPER], int per, int t,
+                                            const RouterParams& p) {
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < KPER; ++j) mx = fmaxf(mx, v[j]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  float denom = 0.f;
+  unsigned key[KPER];
+#pragma unroll
+  for (int j = 0; j < KPER; ++j) {
+    const int i = j * 32 + lane;
+    const bool live = j < per && i < p.E;
+    if (live) denom += expf(v[j] - mx);
+    key[j] = live ? topk_key(v[j], i) : 0u;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) denom += __shfl_xor_sync(0xffffffffu, denom, off);
+  float sel_w = 0.f, sel_sum = 0.f;
+  int sel_id = -1;
+  for (int r = 0; r < p.topk; ++r) {
+    unsigned best = 0u;
+#pragma unroll
+    for (int j = 0; j < KPER; ++j) best = max(best, key[j]);
+    const unsigned win = __reduce_max_sync(0xffffffffu, best);
+    const float pr = expf(topk_key_value(win) - mx) / denom;
+    if (lane == r) { sel_id = 0xffff - (int)(win & 0xffffu); sel_w = pr; }
+    sel_sum += pr;
+#pragma unroll
+    for (int j = 0; j < KPER; ++j)
+      if (key[j] == win) key[j] = 0u;
+  }
+  if (lane < p.topk) {
+    const float wgt = p.renorm ? sel_w / sel_sum : sel_w;
+    p.ids_out[(size_t)t * p.topk + lane] = sel_id;
+    if (p.weights_out) p.weights_out[(size_t)t * p.topk + lane] = wgt;
+    if (p.weights_bf16_out) p.weights_bf16_out[(size_t)t * p.topk + lane] = __float2bfloat16_rn(wgt);
+  }
+}
+
+// ---- decode batches (T <= 2): one cluster of 8 CTAs, no global scratch
+//
+// A decode step routes one token: the 1 MiB gate matrix is split over the 8
+// CTAs of a thread-block cluster (E/8 experts each, two per warp, 16 warps),
+// every logit goes straight into the leader CTA's shared memory over the
+// cluster's distributed shared memory, and after one cluster barrier the
+// leader's warps (one per token) select the top-k.  Compared with the general
+// kernel below this removes the global logit round trip, the fence and the
+// arrival atomic from the critical path.
+constexpr int kRouterClusterCtas = 8;
+constexpr int kRouterClusterThreads = 512;
+// The cluster covers the gate matrix with 8 SMs only, so its fp64 work per SM
+// grows with the token count: measured on B200 it beats the general kernel at
+// 1-2 tokens (10.0 / 13.2 us vs ~14.5 us) and loses from there on.
+constexpr int kRouterClusterMaxT = 2;
+
+__device__ __forceinline__ unsigned cluster_ctarank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(const float* local, unsigned rank, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+// Gate rows of experts eA and eB (eB may be absent): 8 x 16 B per lane each.
+__device__ __forceinline__ void load_gate_pair(const __nv_bfloat16* w, int H, int eA, bool hasB,
+                                               int c0, uint4 (&wa)[8], uint4 (&wb)[8]) {
+  const int vec = H / 8;
+  const uint4* ra = reinterpret_cast<const uint4*>(w + (size_t)eA * H);
+  const uint4* rb = reinterpret_cast<const uint4*>(w + (size_t)(eA + 16) * H);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int c = c0 + 32 * u;
+    wa[u] = c < vec ? __ldg(ra + c) : make_uint4(0, 0, 0, 0);
+    wb[u] = (hasB && c < vec) ? __ldg(rb + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int KPER>
+__global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kernel(RouterParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* s_logits = reinterpret_cast<float*>(smem_raw);  // [8][E], used in the leader
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(
+      smem_raw + (((size_t)kRouterTokensPerCta * p.E * sizeof(float) + 15) & ~(size_t)15));
+  cluster_arrive_relaxed();  // "this CTA has started" (phase 1)
+  const unsigned rank = cluster_ctarank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * kRouterTokensPerCta;
+  const int nt = min(kRouterTokensPerCta, p.T - t0);
+  const int epc = (p.E + kRouterClusterCtas - 1) / kRouterClusterCtas;
+  const int ebase = (int)rank * epc, eend = min(p.E, ebase + epc);
+  const int vec = p.H / 8;
+  // the first gate rows are in flight before the token tile is staged
+  const int eA0 = ebase + warp;
+  uint4 wa[8], wb[8];
+  if (eA0 < eend) load_gate_pair(p.w, p.H, eA0, eA0 + 16 < eend, lane, wa, wb);
+  for (int i = threadIdx.x; i < nt * vec; i += blockDim.x) {
+    const int r = i / vec, c = i - r * vec;
+    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(p.x + (size_t)(t0 + r) * p.H)[c];
+  }
+  __syncthreads();
+  cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
+  for (int eA = eA0; eA < eend; eA += 32) {
+    const bool hasB = eA + 16 < eend;
+    double accA[kRouterTokensPerCta], accB[kRouterTokensPerCta];
+#pragma unroll
+    for (int t = 0; t < kRouterTokensPerCta; ++t) { accA[t] = 0.0; accB[t] = 0.0; }
+    for (int c0 = lane; c0 < vec; c0 += 32 * 8) {
+      if (eA != eA0 || c0 != lane) load_gate_pair(p.w, p.H, eA, hasB, c0, wa, wb);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= vec) break;
+        const __nv_bfloat16* ba = reinterpret_cast<const __nv_bfloat16*>(&wa[u]);
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&wb[u]);
+#pragma unroll
+        for (int t = 0; t < kRouterTokensPerCta; ++t) {
+          if (t < nt) {
+            const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const double xd = (double)__bfloat162float(xb[q]);
+              accA[t] = fma(xd, (double)__bfloat162float(ba[q]), accA[t]);
+              accB[t] = fma(xd, (double)__bfloat162float(bb[q]), accB[t]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterTokensPerCta; ++t) {
+      if (t < nt) {
+        double a = accA[t], b = accB[t];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          a += __shfl_xor_sync(0xffffffffu, a, off);
+          b += __shfl_xor_sync(0xffffffffu, b, off);
+        }
+        if (lane == 0) st_cluster_f32(s_logits + t * p.E + eA, 0, exact_bf16_of(a));
+        if (lane == 0 && hasB) st_cluster_f32(s_logits + t * p.E + eA + 16, 0, exact_bf16_of(b));
+      }
+    }
+  }
+  cluster_arrive_release();  // phase 2: this CTA's logits are in the leader
+  cluster_wait();
+  if (rank != 0 || warp >= nt) return;
+  const int per = (p.E + 31) / 32;
+  float v[KPER];
+#pragma unroll
+  for (int j = 0; j < KPER; ++j) {
+    const int i = j * 32 + lane;
+    v[j] = (j < per && i < p.E) ? s_logits[warp * p.E + i] : -INFINITY;
+  }
+  topk_select<KPER>(v, per, t0 + warp, p);
+}
+
+template <int KPER>
 __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
@@ -125,60 +324,57 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   if (warp < nt) {
     const int t = t0 + warp;
     const float* lg = p.logits + (size_t)t * p.E;
-    constexpr int kPer = kRouterMaxE / 32;
-    float v[kPer];
     const int per = (p.E + 31) / 32;
-    float mx = -INFINITY;
+    float v[KPER];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
+    for (int j = 0; j < KPER; ++j) {
       const int i = j * 32 + lane;
       v[j] = (j < per && i < p.E) ? __ldcg(lg + i) : -INFINITY;
-      mx = fmaxf(mx, v[j]);
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float denom = 0.f;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j)
-      if (j < per && j * 32 + lane < p.E) denom += expf(v[j] - mx);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) denom += __shfl_xor_sync(0xffffffffu, denom, off);
-    float sel_w = 0.f, sel_sum = 0.f;
-    int sel_id = -1;
-    for (int r = 0; r < p.topk; ++r) {
-      // arg-max with lower index winning ties
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int i = j * 32 + lane;
-        if (j < per && i < p.E && (v[j] > bv || (v[j] == bv && i < bi))) { bv = v[j]; bi = i; }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      const float pr = expf(bv - mx) / denom;
-      if (lane == r) { sel_id = bi; sel_w = pr; }
-      sel_sum += pr;
-      // remove the winner
-#pragma unroll
-      for (int j = 0; j < kPer; ++j)
-        if (j * 32 + lane == bi) v[j] = -INFINITY;
-    }
-    if (lane < p.topk) {
-      const float wgt = p.renorm ? sel_w / sel_sum : sel_w;
-      p.ids_out[(size_t)t * p.topk + lane] = sel_id;
-      if (p.weights_out) p.weights_out[(size_t)t * p.topk + lane] = wgt;
-      if (p.weights_bf16_out) p.weights_bf16_out[(size_t)t * p.topk + lane] = __float2bfloat16_rn(wgt);
-    }
+    topk_select<KPER>(v, per, t, p);
   }
   if (threadIdx.x == 0) p.arrivals[blockIdx.y] = 0;  // ready for the next launch / replay
 }
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Launch the router for p (p.arrivals / p.logits already point into the
+// scratch for the general kernel).  T <= kRouterClusterMaxT runs the cluster
+// kernel, which needs no scratch; larger batches the general kernel.
+static int launch_router(const RouterParams& p, cudaStream_t st, const char* what) {
+  const bool small_e = p.E <= 8 * 32;
+  if (p.T <= kRouterClusterMaxT) {
+    const size_t smem = (((size_t)kRouterTokensPerCta * p.E * sizeof(float) + 15) & ~(size_t)15) +
+                        (size_t)kRouterTokensPerCta * p.H * sizeof(__nv_bfloat16);
+    void (*k)(RouterParams) = small_e ? router_cluster_kernel<8> : router_cluster_kernel<32>;
+    if (smem > 48 * 1024)
+      D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "router smem attribute");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kRouterClusterCtas, 1);
+    cfg.blockDim = dim3(kRouterClusterThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kRouterClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    D3_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, p), what);
+    return D3_OK;
+  }
+  const dim3 grid((unsigned)((p.E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
+                  (unsigned)((p.T + kRouterTokensPerCta - 1) / kRouterTokensPerCta));
+  const size_t smem = (size_t)kRouterTokensPerCta * p.H * sizeof(__nv_bfloat16);
+  void (*k)(RouterParams) = small_e ? router_kernel<8> : router_kernel<32>;
+  if (smem > 48 * 1024)
+    D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                "router smem attribute");
+  k<<<grid, 256, smem, st>>>(p);
+  return launch_status(what);
+}
 
 }  // namespace d3
 
@@ -219,15 +415,7 @@ int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int3
   p.ids_out = ids_out;
   p.weights_out = weights_out;
   p.weights_bf16_out = static_cast<__nv_bfloat16*>(weights_bf16_out);
-  const dim3 grid((unsigned)((E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
-                  (unsigned)((T + kRouterTokensPerCta - 1) / kRouterTokensPerCta));
-  const size_t smem = (size_t)kRouterTokensPerCta * H * sizeof(__nv_bfloat16);
-  if (smem > 48 * 1024)
-    D3_CUDA_TRY(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem),
-                "router smem attribute");
-  router_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(p);
-  return launch_status("router_kernel launch");
+  return launch_router(p, (cudaStream_t)stream, "router_kernel launch");
 }
 
 }  // extern "C"
@@ -302,8 +490,9 @@ int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t
   // The arrival counters must start at zero; clear the ones this call uses
   // (a memset on the stream, no allocation).
   const size_t tiles = (size_t)(T + kRouterTokensPerCta - 1) / kRouterTokensPerCta;
-  D3_CUDA_TRY(cudaMemsetAsync(scratch, 0, tiles * sizeof(unsigned), st),
-              "clear router scratch counters");
+  if (T > kRouterClusterMaxT)  // the cluster kernel uses no scratch
+    D3_CUDA_TRY(cudaMemsetAsync(scratch, 0, tiles * sizeof(unsigned), st),
+                "clear router scratch counters");
   RouterParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.w = static_cast<const __nv_bfloat16*>(gate_w);
@@ -313,15 +502,7 @@ int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t
   p.ids_out = ids_out;
   p.weights_out = weights_out;
   p.weights_bf16_out = static_cast<__nv_bfloat16*>(weights_bf16_out);
-  const dim3 grid((unsigned)((E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
-                  (unsigned)tiles);
-  const size_t smem = (size_t)kRouterTokensPerCta * H * sizeof(__nv_bfloat16);
-  if (smem > 48 * 1024)
-    D3_CUDA_TRY(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem),
-                "router smem attribute");
-  router_kernel<<<grid, 256, smem, st>>>(p);
-  return launch_status("router_kernel launch (no-alloc)");
+  return launch_router(p, st, "router_kernel launch (no-alloc)");
 }
 
 }  // extern "C"

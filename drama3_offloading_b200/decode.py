@@ -137,9 +137,8 @@ class DecodeStack:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched per token: router, allocator, fetch,
-        route (with the activation quantisation folded in at batch 1), gemm1,
-        act, gemm2, combine per layer."""
-        return 8 * self.L
+        and the batch-1 expert path's gate/up and down launches per layer."""
+        return 5 * self.L
 
     def roofline_ms(self, hits: float, misses: float, hbm_gbs: float, host_gbs: float) -> float:
         """t >= dense/HBM + hits*expert/HBM + misses*expert/host per token."""

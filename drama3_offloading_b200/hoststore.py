@@ -120,11 +120,21 @@ class SharedHostStore:
         return t
 
     def close(self) -> None:
+        """Unregister every chunk.  Must run before the mapping goes away: a
+        registration left behind after the pages are unmapped makes later
+        copies into host memory that reuses those addresses fail."""
         rt = torch.cuda.cudart() if getattr(self, "chunks", None) else None
         for p in getattr(self, "chunks", []):
             rt.cudaHostUnregister(p)
         self.chunks = []
         self.registered = False
+
+    def __del__(self):
+        # self.mm (the mapping) is released only after this runs
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def layer_bytes(E: int, H: int, I: int) -> int:

@@ -32,7 +32,9 @@ def rel_err(got, ref):
     return float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
 
 
-@pytest.mark.parametrize("T", [1, 16, 100, 2048])
+# T <= 2: one thread-block cluster (logits in distributed shared memory);
+# larger T: the general kernel (logits in the workspace, last CTA selects)
+@pytest.mark.parametrize("T", [1, 2, 5, 8, 9, 16, 100, 2048])
 def test_router_ids_bit_exact(T):
     g = torch.Generator().manual_seed(T)
     x = torch.randn(T, 2048, generator=g).to(torch.bfloat16)
@@ -47,10 +49,11 @@ def test_router_ids_bit_exact(T):
     assert torch.equal(ids2, ids)
 
 
-def test_router_tie_break_lower_index():
+@pytest.mark.parametrize("T", [4, 12])
+def test_router_tie_break_lower_index(T):
     # identical gate rows -> identical logits; ties must resolve to lower ids
     g = torch.Generator().manual_seed(3)
-    x = torch.randn(4, 2048, generator=g).to(torch.bfloat16)
+    x = torch.randn(T, 2048, generator=g).to(torch.bfloat16)
     gw = (torch.randn(256, 2048, generator=g) * 0.02).to(torch.bfloat16)
     # three identical rows aligned with token 0 -> equal top logits for it
     row = (x[0].float().sign() * 0.05).to(torch.bfloat16)
@@ -60,6 +63,19 @@ def test_router_tie_break_lower_index():
     ids, _ = moe.router_topk(x.to(DEV), gw.to(DEV), 8)
     np.testing.assert_array_equal(ids.cpu().numpy(), want_ids.numpy())
     assert ids[0, :3].tolist() == [3, 10, 200]
+
+
+def test_router_cluster_and_general_kernels_agree():
+    """The same tokens routed 2 at a time (cluster kernel) and 16 at a time
+    (general kernel) give identical ids and bit-identical weights."""
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(16, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    gw = (torch.randn(256, 2048, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    ids, w = moe.router_topk(x, gw, 8)
+    parts = [moe.router_topk(x[i:i + 2].contiguous(), gw, 8) for i in range(0, 16, 2)]
+    torch.cuda.synchronize()
+    assert torch.equal(ids, torch.cat([p[0] for p in parts]))
+    assert torch.equal(w, torch.cat([p[1] for p in parts]))
 
 
 @pytest.fixture(scope="module")
@@ -110,10 +126,11 @@ def test_moe_forward_matches_oracle(E, T, k, seed):
     assert rel_err(out, ref) < TOL, rel_err(out, ref)
 
 
-def test_moe_forward_bf16_weights_int64_ids_and_skips():
-    ex, x, ids, w = _rand_case(16, 8, 8, 11, ids_dtype=torch.int64, style="test")
-    ids[2, 3] = -1
-    ids[5, 0] = 16  # out of range -> skipped
+@pytest.mark.parametrize("T", [2, 8])   # CUDA-core path / tensor-core path
+def test_moe_forward_bf16_weights_int64_ids_and_skips(T):
+    ex, x, ids, w = _rand_case(16, T, 8, 11, ids_dtype=torch.int64, style="test")
+    ids[T - 1, 3] = -1
+    ids[0, 0] = 16  # out of range -> skipped
     out = moe.fp8_moe_forward(x.to(DEV), ids.to(DEV), w.to(torch.bfloat16).to(DEV),
                               ex.w13_weight, ex.w13_scale_inv, ex.w2_weight, ex.w2_scale_inv)
     moe.check_errors(DEV)
@@ -190,9 +207,10 @@ def test_dev_cached_forward_equals_resident(cap):
     moe.check_errors(DEV)
 
 
-def test_moe_forward_accumulate_into_input():
+@pytest.mark.parametrize("T", [1, 5])   # CUDA-core path / tensor-core path
+def test_moe_forward_accumulate_into_input(T):
     """accumulate=True with out aliasing x: h <- h + moe(h) (the residual add)."""
-    ex, x, ids, w = _rand_case(16, 3, 8, 41)
+    ex, x, ids, w = _rand_case(16, T, 8, 41)
     xd = x.to(DEV)
     plain = moe.fp8_moe_forward(xd, ids.to(DEV), w.to(DEV), ex.w13_weight, ex.w13_scale_inv,
                                 ex.w2_weight, ex.w2_scale_inv).clone()
@@ -204,7 +222,29 @@ def test_moe_forward_accumulate_into_input():
     assert rel_err(h, want) < 1e-2
 
 
-@pytest.mark.parametrize("E,T,k", [(8, 512, 8), (64, 16, 8), (68, 1, 8)])
+@pytest.mark.parametrize("T", [1, 2, 4])
+def test_moe_small_batch_paths_agree(T, monkeypatch):
+    """Decode-sized batches run on the CUDA cores (GEMV, fp32 activations);
+    forced onto the tensor-core path (D3_GEMV_MAX_PAIRS=0) the same call must
+    agree with it and with the oracle within the tolerance."""
+    ex, x, ids, w = _rand_case(64, T, 8, 50 + T)
+    args = (x.to(DEV), ids.to(DEV), w.to(DEV), ex.w13_weight, ex.w13_scale_inv, ex.w2_weight,
+            ex.w2_scale_inv)
+    gemv = moe.fp8_moe_forward(*args).clone()
+    monkeypatch.setenv("D3_GEMV_MAX_PAIRS", "0")
+    gemm = moe.fp8_moe_forward(*args).clone()
+    moe.check_errors(DEV)
+    cpu = ex.to("cpu")
+    ref = oracle.moe_forward(x, ids, w, cpu.w13_weight, cpu.w13_scale_inv, cpu.w2_weight,
+                             cpu.w2_scale_inv)
+    assert rel_err(gemv, ref) < TOL, rel_err(gemv, ref)
+    assert rel_err(gemm, ref) < TOL, rel_err(gemm, ref)
+    assert rel_err(gemv, gemm) < TOL
+    # the fp32-activation path sits closer to the fp32 oracle
+    assert rel_err(gemv, ref) <= rel_err(gemm, ref) * 1.5 + 1e-3
+
+
+@pytest.mark.parametrize("E,T,k", [(8, 512, 8), (64, 16, 8), (68, 1, 8), (68, 2, 8)])
 def test_moe_forward_deterministic_with_fresh_inputs(E, T, k):
     """Repeated calls, each right after fresh host->device copies of its inputs,
     give bit-identical results (no launch of a call may start before the
