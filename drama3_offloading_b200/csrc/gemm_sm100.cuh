@@ -45,7 +45,7 @@ struct GemmParams {
   const float* xscale;        // [rows][kblocks] activation block scales
   int K;                      // bytes per weight row = K elements
   float* out;                 // [split][P][Mtot]
-  int P, Mtot, kbps;
+  int P, Mtot;
   int* err;                   // device error word (first failure wins)
 };
 
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
         const int4 tl = p.tiles[t];
-        const int e = tl.x, m = tl.y, row0 = tl.z;
+        const int e = tl.x, m = tl.y & 0xffff, row0 = tl.z;
         const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
         const int wrow = e * p.rows_per_expert + m * 128;
         for (int kb = kb0; kb < kb1; kb += KPS) {
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
     uint32_t it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const int4 tl = p.tiles[t];
-      const int e = tl.x, m = tl.y, row0 = tl.z;
+      const int e = tl.x, m = tl.y & 0xffff, row0 = tl.z;
       const int ncount = tl.w & 0xFF;
       const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
       const int nkb = kb1 - kb0;
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
         mbar_arrive(acce + ab);
       }
       if (!ok) continue;  // leaves at the next tile's shared abort decision
-      const int split = kb0 / p.kbps;
+      const int split = tl.y >> 16;  // K-split index of this tile
       float* o = p.out + ((size_t)split * p.P + row0 + col0) * p.Mtot + m * 128 + row;
 #pragma unroll
       for (int n = 0; n < CPT; ++n)

@@ -93,8 +93,11 @@ struct Plan {
   int n;        // experts in the weight arrays
   int H, I;
   int BN;       // pairs per N tile
-  int split1, kbps1;   // gemm1 K split count / K blocks per split (K = H)
-  int split2, kbps2;   // gemm2 (K = I)
+  // K-split bounds: the route launch picks the split from the real tile
+  // count (a sparse batch -- most rows empty, or few pairs per expert -- gets
+  // more K-splits); the workspace holds partials for split*_max splits
+  int split1_min, split1_max;   // gemm1 (K = H)
+  int split2_min, split2_max;   // gemm2 (K = I)
   int maxt1, maxt2;    // tile list capacities
   // workspace offsets (bytes)
   size_t o_cnt, o_off, o_sorted, o_inv, o_tiles1, o_tiles2, o_ntiles, o_xq, o_xs, o_ws1, o_hq,
@@ -110,20 +113,20 @@ static void make_plan(Plan& p, int T, int topk, int n, int H, int I, int sms) {
   p.BN = per_expert > 24.0 ? 64 : 16;
   p.Ppad = (p.P + p.BN - 1) / p.BN * p.BN;
   const int nt_bound = p.P / p.BN + distinct;  // sum_e ceil(c_e / BN)
-  // spread K so that the (experts x M tiles) of a small batch fill the SMs
-  auto split_for = [&](int mtiles, int nkb, int& split, int& kbps) {
-    const long base = (long)(p.P / p.BN + distinct) * mtiles;  // ~tiles without split
-    int want = (int)((2L * sms + base - 1) / (base > 0 ? base : 1));
-    if (want < 1) want = 1;
-    if (want > nkb) want = nkb;
-    kbps = (nkb + want - 1) / want;
-    if (kbps > kGemmMaxTileKb) kbps = kGemmMaxTileKb;  // a tile's scales fit shared memory
-    split = (nkb + kbps - 1) / kbps;
+  // a tile spans at most kGemmMaxTileKb K-blocks (its scales fit shared
+  // memory); up to 8 splits while the partials stay within ~4096 rows x split
+  auto bounds = [&](int nkb, int& lo, int& hi) {
+    lo = (nkb + kGemmMaxTileKb - 1) / kGemmMaxTileKb;
+    int cap = 4096 / (p.P > 0 ? p.P : 1);
+    if (cap > 8) cap = 8;
+    if (cap > nkb) cap = nkb;
+    hi = cap > lo ? cap : lo;
   };
-  split_for(2 * I / 128, H / 128, p.split1, p.kbps1);
-  split_for(H / 128, I / 128, p.split2, p.kbps2);
-  p.maxt1 = nt_bound * (2 * I / 128) * p.split1;
-  p.maxt2 = nt_bound * (H / 128) * p.split2;
+  bounds(H / 128, p.split1_min, p.split1_max);
+  bounds(I / 128, p.split2_min, p.split2_max);
+  (void)sms;
+  p.maxt1 = nt_bound * (2 * I / 128) * p.split1_max;
+  p.maxt2 = nt_bound * (H / 128) * p.split2_max;
   size_t o = 0;
   p.o_cnt = o;     o += al(sizeof(int) * (size_t)n);
   p.o_off = o;     o += al(sizeof(int) * (size_t)n);
@@ -131,13 +134,13 @@ static void make_plan(Plan& p, int T, int topk, int n, int H, int I, int sms) {
   p.o_inv = o;     o += al(sizeof(int) * (size_t)p.P);
   p.o_tiles1 = o;  o += al(sizeof(int4) * (size_t)p.maxt1);
   p.o_tiles2 = o;  o += al(sizeof(int4) * (size_t)p.maxt2);
-  p.o_ntiles = o;  o += al(sizeof(int) * 4);
+  p.o_ntiles = o;  o += al(sizeof(int) * 8);
   p.o_xq = o;      o += al((size_t)p.Ppad * 2 * H);
   p.o_xs = o;      o += al(sizeof(float) * (size_t)p.Ppad * (H / 128));
-  p.o_ws1 = o;     o += al(sizeof(float) * (size_t)p.split1 * p.P * 2 * I);
+  p.o_ws1 = o;     o += al(sizeof(float) * (size_t)p.split1_max * p.P * 2 * I);
   p.o_hq = o;      o += al((size_t)p.Ppad * 2 * I);
   p.o_hs = o;      o += al(sizeof(float) * (size_t)p.Ppad * (I / 128));
-  p.o_ws2 = o;     o += al(sizeof(float) * (size_t)p.split2 * p.P * H);
+  p.o_ws2 = o;     o += al(sizeof(float) * (size_t)p.split2_max * p.P * H);
   p.total = o;
 }
 
@@ -148,8 +151,9 @@ struct RouteParams {
   int* cnt; int* off; int* sorted; int* inv;
   int4* tiles1; int4* tiles2; int* ntiles;
   int BN;
-  int mt1, nkb1, kbps1, split1;
-  int mt2, nkb2, kbps2, split2;
+  int mt1, nkb1, split1_min, split1_max;
+  int mt2, nkb2, split2_min, split2_max;
+  int sms;
   // activation quantisation folded into this launch for small batches
   int fuse_quant;
   const __nv_bfloat16* x; int topk, H, Ppad;
@@ -167,8 +171,21 @@ __device__ __forceinline__ int load_pair_id(const void* ids, int bytes, int i, i
   return (v >= 0 && v < n) ? (int)v : -1;
 }
 
-__device__ __forceinline__ int4 pack_tile(int e, int m, int row0, int ncount, int kb0, int kb1) {
-  return make_int4(e, m, row0, ncount | (kb0 << 8) | (kb1 << 20));
+// Tile: expert, M tile | K-split index << 16, first sorted row,
+// ncount | kb0 << 8 | kb1 << 20.
+__device__ __forceinline__ int4 pack_tile(int e, int m, int split, int row0, int ncount, int kb0,
+                                          int kb1) {
+  return make_int4(e, m | (split << 16), row0, ncount | (kb0 << 8) | (kb1 << 20));
+}
+
+// K-split for `tiles` output tiles of a K range of nkb blocks: enough tiles
+// for ~2 per SM, within [lo, hi]; returns the blocks per split in *kbps.
+__device__ __forceinline__ int pick_split(int tiles, int nkb, int lo, int hi, int sms, int* kbps) {
+  int want = tiles > 0 ? (2 * sms + tiles - 1) / tiles : 1;
+  want = max(lo, min(hi, want));
+  const int per = (nkb + want - 1) / want;
+  *kbps = per;
+  return (nkb + per - 1) / per;
 }
 
 // One CTA of 1024 threads; dynamic smem: cursor[n] + tile prefix[n].
@@ -284,8 +301,14 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
       }
     }
   }
-  // tile lists: for expert e, N tile j, split s, M tile m
-  const int per_nt1 = p.mt1 * p.split1, per_nt2 = p.mt2 * p.split2;
+  // tile lists: for expert e, N tile j, split s, M tile m; the K split from
+  // the real number of N tiles
+  int kbps1, kbps2;
+  const int split1 = pick_split(total_ntiles * p.mt1, p.nkb1, p.split1_min, p.split1_max, p.sms,
+                                &kbps1);
+  const int split2 = pick_split(total_ntiles * p.mt2, p.nkb2, p.split2_min, p.split2_max, p.sms,
+                                &kbps2);
+  const int per_nt1 = p.mt1 * split1, per_nt2 = p.mt2 * split2;
   for (int e = lo; e < hi; ++e) {
     const int c = p.cnt[e];
     if (c == 0) continue;
@@ -295,21 +318,23 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
       const int row0 = p.off[e] + j * p.BN;
       const int nc = min(p.BN, c - j * p.BN);
       int4* d1 = p.tiles1 + (size_t)(t0 + j) * per_nt1;
-      for (int s = 0; s < p.split1; ++s)
+      for (int s = 0; s < split1; ++s)
         for (int m = 0; m < p.mt1; ++m)
-          d1[s * p.mt1 + m] = pack_tile(e, m, row0, nc, s * p.kbps1,
-                                        min(p.nkb1, (s + 1) * p.kbps1));
+          d1[s * p.mt1 + m] = pack_tile(e, m, s, row0, nc, s * kbps1,
+                                        min(p.nkb1, (s + 1) * kbps1));
       int4* d2 = p.tiles2 + (size_t)(t0 + j) * per_nt2;
-      for (int s = 0; s < p.split2; ++s)
+      for (int s = 0; s < split2; ++s)
         for (int m = 0; m < p.mt2; ++m)
-          d2[s * p.mt2 + m] = pack_tile(e, m, row0, nc, s * p.kbps2,
-                                        min(p.nkb2, (s + 1) * p.kbps2));
+          d2[s * p.mt2 + m] = pack_tile(e, m, s, row0, nc, s * kbps2,
+                                        min(p.nkb2, (s + 1) * kbps2));
     }
   }
   if (tid == 0) {
     p.ntiles[0] = total_ntiles * per_nt1;
     p.ntiles[1] = total_ntiles * per_nt2;
     p.ntiles[2] = warp_tot[31];  // valid (in-range) pairs
+    p.ntiles[3] = split1;        // K splits the partial sums come in
+    p.ntiles[4] = split2;
   }
 }
 
@@ -379,10 +404,12 @@ __global__ void quant_x_kernel(const __nv_bfloat16* x, const int* sorted, const 
 
 // One warp per (sorted row, K block of I) of the valid rows: sum splits,
 // SwiGLU, quantise.
-__global__ void act_kernel(const float* ws1, int split, int P, int Ppad, const int* nvalid_ptr,
-                           int I, uint8_t* __restrict__ hq, float* __restrict__ hs) {
+__global__ void act_kernel(const float* ws1, const int* split_ptr, int P, int Ppad,
+                           const int* nvalid_ptr, int I, uint8_t* __restrict__ hq,
+                           float* __restrict__ hs) {
   pdl_trigger();
   pdl_wait();
+  const int split = *split_ptr;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int nkb = I / 128;
   if (gw >= *nvalid_ptr * nkb) return;
@@ -408,11 +435,12 @@ __global__ void act_kernel(const float* ws1, int split, int P, int Ppad, const i
 }
 
 // out[t, j] = bf16( [out[t,j] +] sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
-__global__ void combine_kernel(const float* ws2, int split, int P, int H, const int* inv,
-                               const void* weights, int weights_f32, int T, int topk,
-                               int accumulate, __nv_bfloat16* out) {
+__global__ void combine_kernel(const float* ws2, const int* split_ptr, int P, int H,
+                               const int* inv, const void* weights, int weights_f32, int T,
+                               int topk, int accumulate, __nv_bfloat16* out) {
   pdl_trigger();
   pdl_wait();
+  const int split = *split_ptr;
   const int t = blockIdx.y;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || j >= H) return;
@@ -578,8 +606,11 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   rp.tiles1 = (int4*)(ws + pl.o_tiles1); rp.tiles2 = (int4*)(ws + pl.o_tiles2);
   rp.ntiles = (int*)(ws + pl.o_ntiles);
   rp.BN = pl.BN;
-  rp.mt1 = 2 * I / 128; rp.nkb1 = H / 128; rp.kbps1 = pl.kbps1; rp.split1 = pl.split1;
-  rp.mt2 = H / 128; rp.nkb2 = I / 128; rp.kbps2 = pl.kbps2; rp.split2 = pl.split2;
+  rp.mt1 = 2 * I / 128; rp.nkb1 = H / 128;
+  rp.split1_min = pl.split1_min; rp.split1_max = pl.split1_max;
+  rp.mt2 = H / 128; rp.nkb2 = I / 128;
+  rp.split2_min = pl.split2_min; rp.split2_max = pl.split2_max;
+  rp.sms = num_sms();
   uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
   float* xs = (float*)(ws + pl.o_xs);
   // small batches quantise inside the route launch (one CTA, 32 warps)
@@ -613,7 +644,7 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   GemmParams g1{};
   g1.tiles = rp.tiles1; g1.ntiles = rp.ntiles; g1.wscale = s13;
   g1.rows_per_expert = 2 * I; g1.mblocks = 2 * I / 128; g1.kblocks = H / 128;
-  g1.xscale = xs; g1.K = H; g1.out = ws1; g1.P = P; g1.Mtot = 2 * I; g1.kbps = pl.kbps1;
+  g1.xscale = xs; g1.K = H; g1.out = ws1; g1.P = P; g1.Mtot = 2 * I;
   g1.err = err_word;
   rc = pl.BN == 16 ? launch_gemm<16, 2>(tw1, tx1, g1, pl.maxt1, st)
                    : launch_gemm<64, 2>(tw1, tx1, g1, pl.maxt1, st);
@@ -624,7 +655,7 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   {
     const long warps = (long)pl.Ppad * (I / 128);
     D3_CUDA_TRY(launch_k(act_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st,
-                         pdl, (const float*)ws1, pl.split1, P, pl.Ppad,
+                         pdl, (const float*)ws1, (const int*)(rp.ntiles + 3), P, pl.Ppad,
                          (const int*)(rp.ntiles + 2), I, hq, hs),
                 "act_kernel launch");
   }
@@ -634,7 +665,7 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   GemmParams g2{};
   g2.tiles = rp.tiles2; g2.ntiles = rp.ntiles + 1; g2.wscale = s2;
   g2.rows_per_expert = H; g2.mblocks = H / 128; g2.kblocks = I / 128;
-  g2.xscale = hs; g2.K = I; g2.out = ws2; g2.P = P; g2.Mtot = H; g2.kbps = pl.kbps2;
+  g2.xscale = hs; g2.K = I; g2.out = ws2; g2.P = P; g2.Mtot = H;
   g2.err = err_word;
   rc = pl.BN == 16 ? launch_gemm<16, 2>(tw2, tx2, g2, pl.maxt2, st)
                    : launch_gemm<64, 2>(tw2, tx2, g2, pl.maxt2, st);
@@ -642,7 +673,8 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   {
     const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
     D3_CUDA_TRY(launch_k(combine_kernel, grid, dim3(128), 0, st, pdl, (const float*)ws2,
-                         pl.split2, P, H, (const int*)rp.inv, weights, weights_f32, T, topk,
+                         (const int*)(rp.ntiles + 4), P, H, (const int*)rp.inv, weights,
+                         weights_f32, T, topk,
                          accumulate ? 1 : 0, static_cast<__nv_bfloat16*>(out)),
                 "combine_kernel launch");
   }

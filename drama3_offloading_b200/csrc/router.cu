@@ -11,8 +11,8 @@
 // fp64 sum's last bits, so every correct implementation agrees on the ids.
 //
 // Two kernels share the arithmetic and the selection:
-// * T <= 2 (decode): one thread-block cluster of 8 CTAs; each CTA computes
-//   E/8 experts' logits and stores them into the leader CTA's shared memory
+// * T <= 2 (decode): one thread-block cluster of 16 CTAs; each CTA computes
+//   E/16 experts' logits and stores them into the leader CTA's shared memory
 //   over distributed shared memory; after one cluster barrier the leader
 //   selects.  No global scratch.
 // * T > 2: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one expert
@@ -120,21 +120,40 @@ __device__ __forceinline__ void topk_select(const float (&v)[KPER], int per, int
   }
 }
 
-// ---- decode batches (T <= 2): one cluster of 8 CTAs, no global scratch
+// bf16 bit pattern -> the same value as a double, by integer operations:
+// the sign, the exponent rebiased from 127 to 1023 and the 7 mantissa bits
+// placed at the top of the double's mantissa (zeros stay zeros).  Subnormal,
+// infinite and NaN inputs take the conversion instructions instead.  Exact
+// for every input.  Used where each converted weight feeds few products (the
+// decode kernel); where a staged token tile is converted per use the
+// conversion instructions measured faster.
+__device__ __forceinline__ double bf16_bits_to_f64(uint32_t b) {
+  const uint32_t e = b & 0x7f80u;
+  if (e == 0x7f80u || (e == 0u && (b & 0x7fu)))
+    return (double)__uint_as_float(b << 16);
+  const uint32_t mag = b & 0x7fffu;
+  const uint32_t hi = ((b & 0x8000u) << 16) | (mag ? (mag << 13) + (896u << 20) : 0u);
+  return __hiloint2double((int)hi, 0);
+}
+
+// ---- decode batches (T <= 2): one cluster of 16 CTAs, no global scratch
 //
-// A decode step routes one token: the 1 MiB gate matrix is split over the 8
-// CTAs of a thread-block cluster (E/8 experts each, two per warp, 16 warps),
-// every logit goes straight into the leader CTA's shared memory over the
-// cluster's distributed shared memory, and after one cluster barrier the
-// leader's warps (one per token) select the top-k.  Compared with the general
-// kernel below this removes the global logit round trip, the fence and the
-// arrival atomic from the critical path.
-constexpr int kRouterClusterCtas = 8;
+// A decode step routes one token: the 1 MiB gate matrix is split over the 16
+// CTAs of a thread-block cluster (E/16 experts each, one per warp), every
+// logit goes straight into the leader CTA's shared memory over the cluster's
+// distributed shared memory, and after one cluster barrier the leader's warps
+// (one per token) select the top-k.  Compared with the general kernel below
+// this removes the global logit round trip, the fence and the arrival atomic
+// from the critical path.  The token rows are converted to fp64 once per CTA
+// (shared memory, 8-double chunks padded to 10 so the lanes' 16-byte reads
+// hit distinct banks); each gate row's loads are issued before that staging.
+constexpr int kRouterClusterCtas = 16;       // non-portable cluster size (B200 allows 16)
 constexpr int kRouterClusterThreads = 512;
-// The cluster covers the gate matrix with 8 SMs only, so its fp64 work per SM
-// grows with the token count: measured on B200 it beats the general kernel at
-// 1-2 tokens (10.0 / 13.2 us vs ~14.5 us) and loses from there on.
+// The cluster covers the gate matrix with 16 SMs only, so its work per SM
+// grows with the token count; it is used for 1-2 tokens, where it beats the
+// general kernel (measured on B200).
 constexpr int kRouterClusterMaxT = 2;
+constexpr int kRouterXChunk = 10;            // doubles per padded 8-element chunk
 
 __device__ __forceinline__ unsigned cluster_ctarank() {
   unsigned r;
@@ -156,83 +175,85 @@ __device__ __forceinline__ void st_cluster_f32(const float* local, unsigned rank
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
-// Gate rows of experts eA and eB (eB may be absent): 8 x 16 B per lane each.
-__device__ __forceinline__ void load_gate_pair(const __nv_bfloat16* w, int H, int eA, bool hasB,
-                                               int c0, uint4 (&wa)[8], uint4 (&wb)[8]) {
-  const int vec = H / 8;
-  const uint4* ra = reinterpret_cast<const uint4*>(w + (size_t)eA * H);
-  const uint4* rb = reinterpret_cast<const uint4*>(w + (size_t)(eA + 16) * H);
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int c = c0 + 32 * u;
-    wa[u] = c < vec ? __ldg(ra + c) : make_uint4(0, 0, 0, 0);
-    wb[u] = (hasB && c < vec) ? __ldg(rb + c) : make_uint4(0, 0, 0, 0);
-  }
+__host__ __device__ constexpr size_t router_cluster_logit_bytes(int E) {
+  return ((size_t)kRouterClusterMaxT * E * sizeof(float) + 15) & ~(size_t)15;
 }
 
 template <int KPER>
 __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kernel(RouterParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* s_logits = reinterpret_cast<float*>(smem_raw);  // [8][E], used in the leader
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(
-      smem_raw + (((size_t)kRouterTokensPerCta * p.E * sizeof(float) + 15) & ~(size_t)15));
+  float* s_logits = reinterpret_cast<float*>(smem_raw);  // [T][E], used in the leader
+  double* xd = reinterpret_cast<double*>(smem_raw + router_cluster_logit_bytes(p.E));
   cluster_arrive_relaxed();  // "this CTA has started" (phase 1)
   const unsigned rank = cluster_ctarank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.y * kRouterTokensPerCta;
-  const int nt = min(kRouterTokensPerCta, p.T - t0);
+  const int nt = p.T;        // <= kRouterClusterMaxT
+  const int nwarps = kRouterClusterThreads / 32;
   const int epc = (p.E + kRouterClusterCtas - 1) / kRouterClusterCtas;
   const int ebase = (int)rank * epc, eend = min(p.E, ebase + epc);
-  const int vec = p.H / 8;
-  // the first gate rows are in flight before the token tile is staged
-  const int eA0 = ebase + warp;
-  uint4 wa[8], wb[8];
-  if (eA0 < eend) load_gate_pair(p.w, p.H, eA0, eA0 + 16 < eend, lane, wa, wb);
-  for (int i = threadIdx.x; i < nt * vec; i += blockDim.x) {
-    const int r = i / vec, c = i - r * vec;
-    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(p.x + (size_t)(t0 + r) * p.H)[c];
+  const int vec = p.H / 8;   // 8-element chunks per row
+  // this warp's first gate row is in flight before the token rows are staged
+  const int e0 = ebase + warp;
+  uint4 w[8];
+  if (e0 < eend) {
+    const uint4* r = reinterpret_cast<const uint4*>(p.w + (size_t)e0 * p.H);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = lane + 32 * u;
+      w[u] = c < vec ? __ldg(r + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  const uint16_t* xb = reinterpret_cast<const uint16_t*>(p.x);
+  for (int i = threadIdx.x; i < nt * p.H; i += blockDim.x) {
+    const int t = i / p.H, k = i - t * p.H;
+    xd[((size_t)t * vec + (k >> 3)) * kRouterXChunk + (k & 7)] = bf16_bits_to_f64(xb[i]);
   }
   __syncthreads();
   cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
-  for (int eA = eA0; eA < eend; eA += 32) {
-    const bool hasB = eA + 16 < eend;
-    double accA[kRouterTokensPerCta], accB[kRouterTokensPerCta];
-#pragma unroll
-    for (int t = 0; t < kRouterTokensPerCta; ++t) { accA[t] = 0.0; accB[t] = 0.0; }
+  for (int e = e0; e < eend; e += nwarps) {
+    const uint4* r = reinterpret_cast<const uint4*>(p.w + (size_t)e * p.H);
+    double acc[kRouterClusterMaxT] = {0.0, 0.0};
     for (int c0 = lane; c0 < vec; c0 += 32 * 8) {
-      if (eA != eA0 || c0 != lane) load_gate_pair(p.w, p.H, eA, hasB, c0, wa, wb);
+      if (e != e0 || c0 != lane) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = c0 + 32 * u;
+          w[u] = c < vec ? __ldg(r + c) : make_uint4(0, 0, 0, 0);
+        }
+      }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int c = c0 + 32 * u;
         if (c >= vec) break;
-        const __nv_bfloat16* ba = reinterpret_cast<const __nv_bfloat16*>(&wa[u]);
-        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&wb[u]);
+        const uint32_t wr[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+        double wd[8];
 #pragma unroll
-        for (int t = 0; t < kRouterTokensPerCta; ++t) {
+        for (int q = 0; q < 4; ++q) {
+          wd[2 * q] = bf16_bits_to_f64(wr[q] & 0xffffu);
+          wd[2 * q + 1] = bf16_bits_to_f64(wr[q] >> 16);
+        }
+#pragma unroll
+        for (int t = 0; t < kRouterClusterMaxT; ++t) {
           if (t < nt) {
-            const uint4 xv = reinterpret_cast<const uint4*>(xs + t * p.H)[c];
-            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+            const double2* xc =
+                reinterpret_cast<const double2*>(xd + ((size_t)t * vec + c) * kRouterXChunk);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const double xd = (double)__bfloat162float(xb[q]);
-              accA[t] = fma(xd, (double)__bfloat162float(ba[q]), accA[t]);
-              accB[t] = fma(xd, (double)__bfloat162float(bb[q]), accB[t]);
+            for (int q = 0; q < 4; ++q) {
+              const double2 xv = xc[q];
+              acc[t] = fma(xv.x, wd[2 * q], acc[t]);
+              acc[t] = fma(xv.y, wd[2 * q + 1], acc[t]);
             }
           }
         }
       }
     }
 #pragma unroll
-    for (int t = 0; t < kRouterTokensPerCta; ++t) {
+    for (int t = 0; t < kRouterClusterMaxT; ++t) {
       if (t < nt) {
-        double a = accA[t], b = accB[t];
+        double a = acc[t];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          a += __shfl_xor_sync(0xffffffffu, a, off);
-          b += __shfl_xor_sync(0xffffffffu, b, off);
-        }
-        if (lane == 0) st_cluster_f32(s_logits + t * p.E + eA, 0, exact_bf16_of(a));
-        if (lane == 0 && hasB) st_cluster_f32(s_logits + t * p.E + eA + 16, 0, exact_bf16_of(b));
+        for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+        if (lane == 0) st_cluster_f32(s_logits + t * p.E + e, 0, exact_bf16_of(a));
       }
     }
   }
@@ -246,7 +267,7 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
     const int i = j * 32 + lane;
     v[j] = (j < per && i < p.E) ? s_logits[warp * p.E + i] : -INFINITY;
   }
-  topk_select<KPER>(v, per, t0 + warp, p);
+  topk_select<KPER>(v, per, warp, p);
 }
 
 template <int KPER>
@@ -344,9 +365,11 @@ static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 static int launch_router(const RouterParams& p, cudaStream_t st, const char* what) {
   const bool small_e = p.E <= 8 * 32;
   if (p.T <= kRouterClusterMaxT) {
-    const size_t smem = (((size_t)kRouterTokensPerCta * p.E * sizeof(float) + 15) & ~(size_t)15) +
-                        (size_t)kRouterTokensPerCta * p.H * sizeof(__nv_bfloat16);
+    const size_t smem = router_cluster_logit_bytes(p.E) +
+                        (size_t)kRouterClusterMaxT * (p.H / 8) * kRouterXChunk * sizeof(double);
     void (*k)(RouterParams) = small_e ? router_cluster_kernel<8> : router_cluster_kernel<32>;
+    D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "router cluster-size attribute");
     if (smem > 48 * 1024)
       D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                   "router smem attribute");

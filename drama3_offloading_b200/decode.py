@@ -12,7 +12,7 @@ Per layer and decode token (batch 1):
 2. router ``d3_router_topk`` on the layer's bf16 gate [256, 2048].
 3. ``d3_resolve_fetch``: device slot allocator + fetch of the missed experts
    from pinned host memory into the layer's device cache.
-4. ``d3_moe_fp8_forward`` on the cache slots, then ``h = rms(h + moe)``.
+4. ``d3_moe_fp8_forward`` on the cache slots, accumulated into ``h``.
 
 Routing: the router runs every layer (its cost is real), but the expert ids
 fed to the cache come from the seeded Zipf(1.1) trace so hit rates are those

@@ -65,6 +65,27 @@ def test_router_tie_break_lower_index(T):
     assert ids[0, :3].tolist() == [3, 10, 200]
 
 
+@pytest.mark.parametrize("T", [1, 5])
+def test_router_exact_with_zeros_and_subnormals(T):
+    """bf16 -> fp64 conversion by bit manipulation: zeros (both signs) and
+    subnormal inputs still give the oracle's ids."""
+    g = torch.Generator().manual_seed(40 + T)
+    x = torch.randn(T, 2048, generator=g)
+    x[:, ::7] = 0.0
+    x[:, 1::13] = -0.0
+    x[:, 3::11] = 1e-39            # bf16 subnormal
+    gw = torch.randn(256, 2048, generator=g) * 0.02
+    gw[:, ::5] = 0.0
+    gw[7, 2::9] = -3e-39
+    x, gw = x.to(torch.bfloat16), gw.to(torch.bfloat16)
+    assert (x.float().abs() < 1.17e-38).logical_and(x.float() != 0).any()
+    want_ids, want_w, _, _ = oracle.router_topk(x, gw, 8)
+    ids, w = moe.router_topk(x.to(DEV), gw.to(DEV), 8)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids.cpu().numpy(), want_ids.numpy())
+    np.testing.assert_allclose(w.cpu().numpy(), want_w.numpy(), rtol=1e-5, atol=1e-7)
+
+
 def test_router_cluster_and_general_kernels_agree():
     """The same tokens routed 2 at a time (cluster kernel) and 16 at a time
     (general kernel) give identical ids and bit-identical weights."""
