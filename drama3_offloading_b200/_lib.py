@@ -61,10 +61,14 @@ SIGNATURES: dict[str, tuple] = {
     "d3_moe_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "d3_moe_fp8_forward": (ctypes.c_int, [P, P, I32, P, I32, I32, I32, P, P, P, P, I32, I32,
                                           I32, P, I32, P, P, SZ, P]),
+    "d3_moe_fp8_forward_shared": (ctypes.c_int, [P, P, I32, P, I32, I32, I32, P, P, P, P, I32,
+                                                 I32, I32, P, P, P, P, I32, P, P, SZ, P]),
     "d3_prefill_plan": (ctypes.c_int, [P, I32, I32, I32, P, P, P, P, P]),
     "d3_gather_experts": (ctypes.c_int, [ctypes.POINTER(LayerCache), P, P, P, P, I32, P]),
     "d3_ep_dispatch_pack":(ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P]),
     "d3_ep_combine": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, I32, P]),
+    "d3_census_add": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, P]),
+    "d3_trace_append": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, I64, P]),
 }
 
 _lib = None

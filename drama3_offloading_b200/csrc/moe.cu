@@ -491,11 +491,14 @@ static int gemv_max_pairs() {
 
 static size_t gemv2_smem(int topk, int I) { return (size_t)topk * (I / 16) * 20 * sizeof(float); }
 
-static bool gemv_supported(int P, int topk, int H, int I) {
+static bool gemv_shapes_ok(int topk, int H, int I) {
   const int c1 = H / 512, c2 = I / 512;
-  return P <= gemv_max_pairs() && H % 512 == 0 && I % 512 == 0 &&
-         (c1 == 1 || c1 == 2 || c1 == 4 || c1 == 8) && (c2 == 1 || c2 == 2 || c2 == 4) &&
-         gemv2_smem(topk, I) <= 96 * 1024;
+  return H % 512 == 0 && I % 512 == 0 && (c1 == 1 || c1 == 2 || c1 == 4 || c1 == 8) &&
+         (c2 == 1 || c2 == 2 || c2 == 4) && gemv2_smem(topk + 1, I) <= 96 * 1024;
+}
+
+static bool gemv_supported(int P, int topk, int H, int I) {
+  return P <= gemv_max_pairs() && gemv_shapes_ok(topk, H, I);
 }
 
 template <int C1>
@@ -531,7 +534,7 @@ static int run_gemv(const GemvParams& gp, cudaStream_t st) {
   int rpw = 1;  // output rows per warp: more once the grid would exceed ~4 CTAs per SM
   while (rpw < 4 && (long)gp.T * gp.H / (kGemvRowsPerCta * rpw) > 4L * sms) rpw *= 2;
   const dim3 grid2((unsigned)(gp.H / (kGemvRowsPerCta * rpw)), (unsigned)gp.T);
-  const size_t smem = gemv2_smem(gp.topk, gp.I);
+  const size_t smem = gemv2_smem(gp.topk + (gp.sw13 ? 1 : 0), gp.I);
   const bool pdl = pdl_enabled();
   switch (gp.I / 512) {
     case 1: e = launch_gemv2<1>(gp, grid2, rpw, smem, st, pdl); break;
@@ -556,11 +559,15 @@ size_t d3_moe_workspace_size(int32_t T, int32_t topk, int32_t n_experts, int32_t
   return p.total;
 }
 
-int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const void* weights,
+}  // extern "C"
+
+// The routed experts, and optionally the shared expert (decode batches only).
+static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const void* weights,
                        int32_t weights_f32, int32_t T, int32_t topk, const void* w13,
                        const float* s13, const void* w2, const float* s2, int32_t n_experts,
                        int32_t H, int32_t I, void* out, int32_t accumulate, int32_t* err_word,
-                       void* workspace, size_t workspace_bytes, d3_stream_t stream) {
+                       void* workspace, size_t workspace_bytes, d3_stream_t stream,
+                       const void* sw13, const void* sw2, const void* sgate) {
   D3_CHECK_ARG(x && ids && weights && w13 && s13 && w2 && s2 && out && err_word,
                "d3_moe_fp8_forward: null pointer");
   D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
@@ -583,9 +590,20 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   cudaStream_t st = (cudaStream_t)stream;
   const int P = pl.P;
 
-  if (gemv_supported(P, topk, H, I)) {
-    // decode-sized batch: two CUDA-core launches; h lives where gemm1's
-    // partials would (split1 * P * 2I floats >= P * I)
+  if (sw13) {
+    D3_CHECK_ARG(sw2 != nullptr, "shared expert: down weights missing");
+    if (!aligned16(sw13) || !aligned16(sw2) || (sgate && !aligned16(sgate)))
+      return fail(D3_ERR_MISALIGNED, "shared expert weights must be 16-byte aligned");
+    if (P > kGemvMaxPairsDefault || !gemv_shapes_ok(topk, H, I))
+      return fail(D3_ERR_UNSUPPORTED,
+                  "the fused shared expert runs on the decode path only (T*topk <= %d, H and I "
+                  "multiples of 512); run it separately for larger batches",
+                  kGemvMaxPairsDefault);
+  }
+  if (sw13 || gemv_supported(P, topk, H, I)) {
+    // decode-sized batch: two CUDA-core launches; h (and the shared expert's
+    // h and gate) live where gemm1's partials would (split1_max * P * 2I
+    // floats >= P * I + T * I + T)
     GemvParams gp{};
     gp.x = static_cast<const __nv_bfloat16*>(x);
     gp.ids = ids; gp.ids_bytes = ids_bytes;
@@ -596,6 +614,11 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
     gp.w2 = static_cast<const uint8_t*>(w2); gp.s2 = s2;
     gp.h = (float*)(ws + pl.o_ws1);
     gp.out = static_cast<__nv_bfloat16*>(out);
+    gp.sw13 = static_cast<const __nv_bfloat16*>(sw13);
+    gp.sw2 = static_cast<const __nv_bfloat16*>(sw2);
+    gp.sgate = static_cast<const __nv_bfloat16*>(sgate);
+    gp.hs = gp.h + (size_t)P * I;
+    gp.gs = gp.hs + (size_t)T * I;
     return run_gemv(gp, st);
   }
 
@@ -679,6 +702,31 @@ int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const 
                 "combine_kernel launch");
   }
   return D3_OK;
+}
+
+extern "C" {
+
+int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes, const void* weights,
+                       int32_t weights_f32, int32_t T, int32_t topk, const void* w13,
+                       const float* s13, const void* w2, const float* s2, int32_t n_experts,
+                       int32_t H, int32_t I, void* out, int32_t accumulate, int32_t* err_word,
+                       void* workspace, size_t workspace_bytes, d3_stream_t stream) {
+  return moe_forward(x, ids, ids_bytes, weights, weights_f32, T, topk, w13, s13, w2, s2,
+                     n_experts, H, I, out, accumulate, err_word, workspace, workspace_bytes,
+                     stream, nullptr, nullptr, nullptr);
+}
+
+int d3_moe_fp8_forward_shared(const void* x, const void* ids, int32_t ids_bytes,
+                              const void* weights, int32_t weights_f32, int32_t T, int32_t topk,
+                              const void* w13, const float* s13, const void* w2, const float* s2,
+                              int32_t n_experts, int32_t H, int32_t I, const void* shared_w13,
+                              const void* shared_w2, const void* shared_gate, void* out,
+                              int32_t accumulate, int32_t* err_word, void* workspace,
+                              size_t workspace_bytes, d3_stream_t stream) {
+  D3_CHECK_ARG(shared_w13 && shared_w2, "d3_moe_fp8_forward_shared: null shared expert");
+  return moe_forward(x, ids, ids_bytes, weights, weights_f32, T, topk, w13, s13, w2, s2,
+                     n_experts, H, I, out, accumulate, err_word, workspace, workspace_bytes,
+                     stream, shared_w13, shared_w2, shared_gate);
 }
 
 }  // extern "C"

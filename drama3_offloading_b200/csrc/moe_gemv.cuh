@@ -20,6 +20,12 @@
 //            on gemv13, so with programmatic launch the down-projection weights
 //            stream in while the gate/up products finish.
 //
+// Optional shared expert (Drama-3's per-layer bf16 SwiGLU expert that every
+// token runs, gated by sigmoid(x . shared_expert_gate)): gemv13 also runs its
+// (token, row) units and one gate unit per token; gemv2 adds
+// sigmoid(x . g) * (W2s[j] . hs[t]) to the same output in the same warp, so
+// the whole MoE block is the same two launches.
+//
 // Activations stay fp32/bf16 (no activation quantisation), so this path is
 // at least as accurate as the tensor-core path; both sum the same products.
 // Ids outside [0, n) skip their pair, as everywhere in this library.
@@ -49,6 +55,13 @@ struct GemvParams {
   const float* s2;          // [n, H/128, I/128]
   float* h;                 // [T*topk, I] workspace
   __nv_bfloat16* out;       // [T, H]
+  // optional shared expert (every token, bf16, intermediate I): null sw13 =
+  // none; null sgate = ungated
+  const __nv_bfloat16* sw13;   // [2I, H] (gate rows [0, I), up rows [I, 2I))
+  const __nv_bfloat16* sw2;    // [H, I]
+  const __nv_bfloat16* sgate;  // [H]
+  float* hs;                   // [T, I] workspace
+  float* gs;                   // [T] workspace: sigmoid(x . sgate)
 };
 
 __device__ __forceinline__ int gemv_pair_id(const void* ids, int bytes, int i, int n) {
@@ -77,6 +90,18 @@ __device__ __forceinline__ float dot16_e4m3(const uint4 w, const float (&v)[16])
   return s0 + s1;
 }
 
+// sum_q w[q] * v[q] over 16 bf16 weights (two 16-byte words), two partial sums.
+__device__ __forceinline__ float dot16_bf16(const uint4 a, const uint4 b, const float (&v)[16]) {
+  const uint32_t wr[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    s0 = fmaf(__uint_as_float(wr[q] << 16), v[2 * q], s0);
+    s1 = fmaf(__uint_as_float(wr[q] & 0xffff0000u), v[2 * q + 1], s1);
+  }
+  return s0 + s1;
+}
+
 __device__ __forceinline__ void unpack_bf16x8(const uint4 r, float* v) {
   const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
@@ -101,10 +126,52 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) 
   const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long nw = ((long)gridDim.x * blockDim.x) >> 5;
   const int I = p.I, H = p.H, nkb = H / 128;
-  const long units = (long)p.T * p.topk * I;
+  const long routed = (long)p.T * p.topk * I;
+  // after the routed (pair, row) units: the shared expert's (token, row)
+  // units, then one gate unit per token
+  const long units = routed + (p.sw13 ? (long)p.T * I + (p.sgate ? p.T : 0) : 0);
   float xv[CPL][16];
   int cur_t = -1;
   for (long u = gw; u < units; u += nw) {
+    if (u >= routed) {  // shared expert (warp-uniform branch)
+      const long v = u - routed;
+      const bool gate_unit = v >= (long)p.T * I;
+      const int t = gate_unit ? (int)(v - (long)p.T * I) : (int)(v / I);
+      const int j = gate_unit ? 0 : (int)(v - (long)t * I);
+      if (t != cur_t) {
+        cur_t = t;
+        const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * H);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int q = lane + 32 * c;
+          unpack_bf16x8(xr[2 * q], xv[c]);
+          unpack_bf16x8(xr[2 * q + 1], xv[c] + 8);
+        }
+      }
+      const uint4* rg = reinterpret_cast<const uint4*>(gate_unit ? p.sgate
+                                                                 : p.sw13 + (size_t)j * H);
+      float ag = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int q = lane + 32 * c;
+        ag += dot16_bf16(__ldcg(rg + 2 * q), __ldcg(rg + 2 * q + 1), xv[c]);
+      }
+      ag = warp_sum(ag);
+      if (gate_unit) {
+        if (lane == 0) p.gs[t] = 1.f / (1.f + expf(-ag));
+        continue;
+      }
+      const uint4* ru = reinterpret_cast<const uint4*>(p.sw13 + (size_t)(I + j) * H);
+      float au = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int q = lane + 32 * c;
+        au += dot16_bf16(__ldcg(ru + 2 * q), __ldcg(ru + 2 * q + 1), xv[c]);
+      }
+      au = warp_sum(au);
+      if (lane == 0) p.hs[(size_t)t * I + j] = ag / (1.f + expf(-ag)) * au;
+      continue;
+    }
     const int pair = (int)(u / I), j = (int)(u - (long)pair * I);
     const int e = gemv_pair_id(p.ids, p.ids_bytes, pair, p.n);
     if (e < 0) continue;  // warp-uniform: the whole warp works on one unit
@@ -143,8 +210,9 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) 
 }
 
 // CPL = 16-byte chunks per lane of a W2 row = I / 512.  Grid (H / 8 / rpw, T);
-// dynamic shared memory: topk rows of h, each 16-float chunk padded to 20
-// floats (conflict-free 16-byte reads: lane l's chunk starts at bank 20 l).
+// dynamic shared memory: topk rows of h (+ the shared expert's row), each
+// 16-float chunk padded to 20 floats (conflict-free 16-byte reads: lane l's
+// chunk starts at bank 20 l).
 template <int CPL>
 __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, int rpw) {
   constexpr int kGemvPairGroup = 8 / CPL;  // W2 rows (of pairs) a warp keeps in flight
@@ -170,13 +238,27 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
       for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
     }
   }
+  // the shared expert's first down row too (bf16: two 16-byte words per chunk)
+  uint4 sw0[CPL][2];
+  if (p.sw13 && j_first < H) {
+    const uint4* wr = reinterpret_cast<const uint4*>(p.sw2 + (size_t)j_first * I);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      sw0[c][0] = __ldcg(wr + 2 * (lane + 32 * c));
+      sw0[c][1] = __ldcg(wr + 2 * (lane + 32 * c) + 1);
+    }
+  }
   pdl_wait();
-  // stage the token's pair rows of h (written by the gate/up launch)
-  for (int i = threadIdx.x; i < topk * (I / 4); i += blockDim.x) {
+  // stage the token's pair rows of h (written by the gate/up launch), and the
+  // shared expert's row as row topk
+  const int nrows = topk + (p.sw13 ? 1 : 0);
+  for (int i = threadIdx.x; i < nrows * (I / 4); i += blockDim.x) {
     const int k = i / (I / 4), f4 = i - k * (I / 4);
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)(t * topk + k) * I) + f4);
+    const float* src = k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I;
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + f4);
     *reinterpret_cast<float4*>(s_h + k * row_stride + (f4 >> 2) * 20 + (f4 & 3) * 4) = v;
   }
+  const float sgate = (p.sw13 && p.sgate) ? __ldcg(p.gs + t) : 1.f;
   if (threadIdx.x < topk) {
     const int i = t * topk + threadIdx.x;
     s_e[threadIdx.x] = gemv_pair_id(p.ids, p.ids_bytes, i, p.n);
@@ -229,6 +311,33 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
         }
         acc = fmaf(s_w[k], part, acc);
       }
+    }
+    if (p.sw13) {  // shared expert: acc += sigmoid gate * (W2s[j] . hs[t])
+      uint4 sw[CPL][2];
+      if (r == 0) {
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) { sw[c][0] = sw0[c][0]; sw[c][1] = sw0[c][1]; }
+      } else {
+        const uint4* wr = reinterpret_cast<const uint4*>(p.sw2 + (size_t)j * I);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          sw[c][0] = __ldcg(wr + 2 * (lane + 32 * c));
+          sw[c][1] = __ldcg(wr + 2 * (lane + 32 * c) + 1);
+        }
+      }
+      float part = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const float* hp = s_h + topk * row_stride + (lane + 32 * c) * 20;
+        float hv[16];
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+          const float4 a = *reinterpret_cast<const float4*>(hp + 4 * f);
+          hv[4 * f] = a.x; hv[4 * f + 1] = a.y; hv[4 * f + 2] = a.z; hv[4 * f + 3] = a.w;
+        }
+        part += dot16_bf16(sw[c][0], sw[c][1], hv);
+      }
+      acc = fmaf(sgate, part, acc);
     }
     acc = warp_sum(acc);
     if (lane == 0) {

@@ -77,15 +77,25 @@ def workspace_bytes(T: int, topk: int, n_experts: int, H: int, I: int) -> int:
     return int(_lib.load().d3_moe_workspace_size(T, topk, n_experts, H, I))
 
 
+SHARED_FUSED_MAX_PAIRS = 32   # the decode (GEMV) path of the library
+
+
 def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                     w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
                     out: torch.Tensor | None = None, accumulate: bool = False,
-                    stream=None) -> torch.Tensor:
+                    stream=None, shared: tuple | None = None) -> torch.Tensor:
     """Routed MoE over block-scaled FP8 experts; returns bf16 [T, H].
 
     ids (int32/int64) out of range -- e.g. -1 -- contribute nothing.  With
     ``accumulate=True`` the result is added to ``out`` (which may be ``x``
-    itself: the block's residual add)."""
+    itself: the block's residual add).
+
+    ``shared=(w13_s, w2_s, gate_s)`` adds Drama-3's shared expert: bf16
+    w13_s [2I, H] (gate rows, then up rows), w2_s [H, I], gate_s [H] or None,
+    ``sigmoid(x . gate_s) * w2_s(silu(x w_g^T) * (x w_u^T))``.  Decode batches
+    run it inside the same two launches as the routed experts
+    (``d3_moe_fp8_forward_shared``); larger batches add it with two plain
+    bf16 GEMMs (cuBLAS) after the routed call."""
     if x.dtype != torch.bfloat16:
         raise TypeError("x must be bf16")
     x = x.contiguous()
@@ -121,8 +131,38 @@ def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     if need == 0:
         raise ValueError(f"unsupported MoE shape T={T} topk={topk} n={n} H={H} I={I}")
     ws = _workspace(dev, need, "moe")
+    wf = 1 if weights.dtype == torch.float32 else 0
+    if shared is not None:
+        sw13, sw2, sg = shared
+        for t, name in ((sw13, "w13_s"), (sw2, "w2_s")):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous():
+                raise TypeError(f"shared expert {name} must be contiguous bf16")
+        if tuple(sw13.shape) != (2 * I, H) or tuple(sw2.shape) != (H, I):
+            raise ValueError("shared expert shapes must be w13_s [2I, H] and w2_s [H, I]")
+        if sg is not None:
+            sg = sg.reshape(H).contiguous()
+        if T * topk <= SHARED_FUSED_MAX_PAIRS and H % 512 == 0 and I % 512 == 0:
+            _lib.call("d3_moe_fp8_forward_shared", _lib.ptr(x), _lib.ptr(ids),
+                      ids.element_size(), _lib.ptr(weights), wf, T, topk, _lib.ptr(w13),
+                      _lib.ptr(s13), _lib.ptr(w2), _lib.ptr(s2), n, H, I, _lib.ptr(sw13),
+                      _lib.ptr(sw2), _lib.ptr(sg) if sg is not None else None, _lib.ptr(out),
+                      1 if accumulate else 0, _lib.ptr(error_word(dev)), _lib.ptr(ws),
+                      ws.numel(), _lib.stream_ptr(stream))
+            return out
+        # larger batches: the routed experts, then the shared expert as two
+        # plain bf16 GEMMs (library GEMMs) added in fp32
+        y = torch.nn.functional.linear(x, sw13).float()
+        hs = torch.nn.functional.silu(y[:, :I]) * y[:, I:]
+        ys = torch.nn.functional.linear(hs.to(torch.bfloat16), sw2).float()
+        if sg is not None:
+            ys = ys * torch.sigmoid(x.float() @ sg.float())[:, None]
+        base = out.float() if accumulate else torch.zeros_like(ys)
+        fp8_moe_forward(x, ids, weights, w13, s13, w2, s2, out=out, accumulate=False,
+                        stream=stream)
+        out.copy_((base + out.float() + ys).to(torch.bfloat16))
+        return out
     _lib.call("d3_moe_fp8_forward", _lib.ptr(x), _lib.ptr(ids), ids.element_size(),
-              _lib.ptr(weights), 1 if weights.dtype == torch.float32 else 0, T, topk,
+              _lib.ptr(weights), wf, T, topk,
               _lib.ptr(w13), _lib.ptr(s13), _lib.ptr(w2), _lib.ptr(s2), n, H, I, _lib.ptr(out),
               1 if accumulate else 0, _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(),
               _lib.stream_ptr(stream))

@@ -15,6 +15,16 @@ parts of the reference's ``bin/offload.py``.
 
 Gather counts are kept on the device (``gather_counters(experts)``) rather
 than as host-side STATS increments, which would need a sync.
+
+Routing observability (bin/offload.py:40-79, :257-287): ``TRACE``
+(``RouterTrace``: ``enabled``, ``add``, ``records``, ``save``,
+``first_decode``) and ``enable_census`` / ``CENSUS`` / ``CENSUS_DECODE`` keep
+the reference's names, but the ids never leave the device on the hot path:
+the census is an int64 [layers, experts] device tensor updated by
+``d3_census_add`` and the trace a device ring filled by ``d3_trace_append``.
+Both are read (one sync) only when the host asks.  Calls hook them at the top
+of ``offloaded_forward``, as the reference does (its device-cache decode path
+is not traced either).
 """
 from __future__ import annotations
 
@@ -33,6 +43,108 @@ STATS = {"experts_copied": 0, "bytes_copied": 0, "hits": 0, "misses": 0,
          "gather_hits": 0, "gather_misses": 0}
 
 _BUF: dict = {}
+
+
+# ---------------------------------------------------------------- trace
+
+class RouterTrace:
+    """Every (layer, routed row) -> its top-k expert ids, in a device ring.
+
+    ``add`` launches one kernel (no host sync, graph-capturable); ``records``
+    reads the ring back and groups rows into the reference's per-call records
+    ``{"phase": "decode"|"prefill", "layer": l, "ids": [[...], ...]}`` (a call
+    of one row is decode).  ``capacity`` rows are kept; older rows are
+    overwritten and ``dropped`` counts them."""
+
+    def __init__(self, capacity: int = 1 << 16) -> None:
+        self.enabled = True
+        self.phase = "prefill"
+        self.first_decode: float | None = None
+        self.capacity = capacity
+        self._ring = None
+        self._cursor = None
+        self._k = None
+
+    def _alloc(self, device, k: int) -> None:
+        if self._ring is None or self._ring.device != device or self._k != k:
+            self._k = k
+            self._ring = torch.zeros(self.capacity, 3 + k, dtype=torch.int32, device=device)
+            self._cursor = torch.zeros(1, dtype=torch.int64, device=device)
+
+    def add(self, layer: int, topk_ids: torch.Tensor) -> None:
+        if not self.enabled:
+            return
+        rows, k = topk_ids.shape
+        if rows == 1 and self.first_decode is None:
+            self.first_decode = time.perf_counter()
+        self._alloc(topk_ids.device, k)
+        ids = topk_ids.contiguous()
+        _lib.call("d3_trace_append", _lib.ptr(ids), ids.element_size(), rows, k, int(layer),
+                  _lib.ptr(self._ring), _lib.ptr(self._cursor), self.capacity,
+                  _lib.stream_ptr())
+
+    @property
+    def dropped(self) -> int:
+        if self._cursor is None:
+            return 0
+        return max(0, int(self._cursor.item()) - self.capacity)
+
+    @property
+    def records(self) -> list:
+        if self._cursor is None:
+            return []
+        n = int(self._cursor.item())
+        first = max(0, n - self.capacity)
+        ring = self._ring.cpu()
+        out, cur = [], None
+        for r in range(first, n):
+            row = ring[r % self.capacity].tolist()
+            call, layer, phase, ids = row[0], row[1], row[2], row[3:]
+            if cur is None or cur[0] != call:
+                cur = (call, {"phase": "decode" if phase else "prefill", "layer": layer,
+                              "ids": []})
+                out.append(cur[1])
+            cur[1]["ids"].append(ids)
+        return out
+
+    def save(self, path, meta: dict) -> None:
+        import json
+        from pathlib import Path
+        Path(path).write_text(json.dumps({"meta": meta, "records": self.records}))
+
+
+TRACE = RouterTrace()
+
+
+# ---------------------------------------------------------------- census
+# [layer, expert] call counts, prefill and decode together, and decode alone
+# (one routed row); int64 device tensors (``.tolist()`` / ``.cpu()`` to read).
+CENSUS = None
+CENSUS_DECODE = None
+
+
+def enable_census(layers: int = 40, experts: int = 256, device=None) -> None:
+    global CENSUS, CENSUS_DECODE
+    dev = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    CENSUS = torch.zeros(layers, experts, dtype=torch.int64, device=dev)
+    CENSUS_DECODE = torch.zeros(layers, experts, dtype=torch.int64, device=dev)
+
+
+def _count(layer: int, topk_ids: torch.Tensor) -> None:
+    if CENSUS is None or layer < 0:
+        return
+    rows, k = topk_ids.shape
+    ids = topk_ids.contiguous()
+    _lib.call("d3_census_add", _lib.ptr(ids), ids.element_size(), rows, k, CENSUS.shape[1],
+              _lib.ptr(CENSUS[layer]), _lib.ptr(CENSUS_DECODE[layer]), _lib.stream_ptr())
+
+
+def observe(experts, topk_ids: torch.Tensor) -> None:
+    """Census and trace of one MoE call (bin/offload.py:139-140)."""
+    layer = getattr(experts, "_layer_index", -1)
+    _count(layer, topk_ids)
+    TRACE.add(layer, topk_ids)
 
 
 def _buffers(experts, device):
@@ -85,6 +197,7 @@ def gather_counters(experts) -> dict:
 
 def offloaded_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
     """MoE forward for experts held in pinned host memory (any number of rows)."""
+    observe(self, topk_ids)
     if self.w13_weight.device.type != "cpu":
         return moe.fp8_moe_forward(x, topk_ids, topk_weights, self.w13_weight,
                                    self.w13_scale_inv, self.w2_weight, self.w2_scale_inv)
@@ -153,8 +266,15 @@ def size_cache_to_free_vram(model, device, leave_free_gib: float = 2.0,
     return capacity
 
 
-def install_offload(experts_cls) -> None:
+def install_offload(experts_cls, model=None) -> None:
     """Route ``experts_cls.forward`` through offloaded_forward, keeping the
-    stock forward as ``_stock_forward`` (bin/offload.py:702-704)."""
+    stock forward as ``_stock_forward`` (bin/offload.py:702-704).  With the
+    model given, every layer's experts also get ``_layer_index`` (the census
+    and trace key, bin/offload.py:128)."""
     experts_cls._stock_forward = experts_cls.forward
     experts_cls.forward = offloaded_forward
+    if model is not None:
+        for index, layer in enumerate(model.backbone.model.layers):
+            experts = getattr(layer.mlp, "experts", None)
+            if experts is not None:
+                experts._layer_index = index

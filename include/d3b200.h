@@ -226,6 +226,24 @@ D3_API int d3_moe_fp8_forward(const void* x, const void* ids, int32_t ids_bytes,
                               int32_t accumulate, int32_t* err_word, void* workspace,
                               size_t workspace_bytes, d3_stream_t stream);
 
+/* d3_moe_fp8_forward plus Drama-3's shared expert in the same two launches:
+ * every token also runs the bf16 SwiGLU expert shared_w13 [2I, H] (gate rows
+ * [0, I), up rows [I, 2I)), shared_w2 [H, I], scaled by
+ * sigmoid(x . shared_gate) (shared_gate [H] bf16; null = ungated), all added
+ * into out.  Decode batches only (T * topk <= 32, H and I multiples of 512);
+ * larger batches -> D3_ERR_UNSUPPORTED (run the shared expert as a plain
+ * dense GEMM).  The upstream MoE block computes the shared expert with its
+ * own bf16 Linear layers outside the offloaded path (notes/01-static-
+ * findings.md:80-82; shared_expert_gate: notes/drama3-config.json:215). */
+D3_API int d3_moe_fp8_forward_shared(const void* x, const void* ids, int32_t ids_bytes,
+                                     const void* weights, int32_t weights_f32, int32_t T,
+                                     int32_t topk, const void* w13, const float* s13,
+                                     const void* w2, const float* s2, int32_t n_experts,
+                                     int32_t H, int32_t I, const void* shared_w13,
+                                     const void* shared_w2, const void* shared_gate, void* out,
+                                     int32_t accumulate, int32_t* err_word, void* workspace,
+                                     size_t workspace_bytes, d3_stream_t stream);
+
 /* ---------------------------------------------------- expert parallelism */
 
 /* Build the static-capacity all-to-all send buffer for expert parallelism
@@ -249,6 +267,30 @@ D3_API int d3_ep_dispatch_pack(const void* x, const int32_t* ids, int32_t T, int
 D3_API int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
                          int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
                          int32_t accumulate, d3_stream_t stream);
+
+/* ---------------------------------------------------------------- routing census / trace */
+
+/* counts[e] += occurrences of expert e among the rows*k ids (int32 or int64,
+ * ids_bytes 4 or 8; ids outside [0, num_experts) are not counted); a call of
+ * exactly one row (a decode step) also adds to counts_decode when that is
+ * non-null.  counts / counts_decode: this layer's int64 [num_experts] rows of
+ * the census.  Device-side, sync-free and graph-capturable.  Replaces the
+ * reference's host-side census (bin/offload.py:257-287 enable_census / _count,
+ * which copies the ids to the CPU on every call). */
+D3_API int d3_census_add(const void* ids, int32_t ids_bytes, int32_t rows, int32_t k,
+                         int32_t num_experts, int64_t* counts, int64_t* counts_decode,
+                         d3_stream_t stream);
+
+/* Router trace: appends one record per row to a device ring of `capacity`
+ * records of 3 + k int32 each: {first row index of this call (low 31 bits of
+ * the cursor), layer, phase (1 if the call has exactly one row -- decode --
+ * else 0), ids[k]}.  *cursor (int64, device) counts every row ever appended;
+ * record r lives at ring[(r % capacity) * (3 + k)].  rows > capacity ->
+ * D3_ERR_TOO_LARGE.  Replaces bin/offload.py:40-79 RouterTrace.add (host
+ * lists, a device sync per call). */
+D3_API int d3_trace_append(const void* ids, int32_t ids_bytes, int32_t rows, int32_t k,
+                           int32_t layer, int32_t* ring, int64_t* cursor, int64_t capacity,
+                           d3_stream_t stream);
 
 #ifdef __cplusplus
 }

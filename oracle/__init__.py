@@ -26,6 +26,8 @@ Contents and what each follows:
   top-k sum.  The upstream module (fish-speech @ 5415669) is not vendored in
   the reference, so the absolute MoE numerics are PARITY UNPINNED: only the
   cache/fetch/slot semantics above are pinned to the reference's own code.
+* ``shared_expert_forward`` -- Drama-3's per-layer bf16 shared expert with its
+  sigmoid gate (inferred from the config, see the function), fp32.
 """
 from __future__ import annotations
 
@@ -43,7 +45,7 @@ _LIB = None
 __all__ = [
     "lib", "init_tables", "resolve", "resolve_lfu", "fetch", "replay",
     "bf16_round", "router_logits", "router_topk", "dequantize_fp8_blocks",
-    "quantize_fp8_blocks", "moe_forward",
+    "quantize_fp8_blocks", "moe_forward", "shared_expert_forward",
 ]
 
 
@@ -246,3 +248,22 @@ def moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, w13: 
         wk = weights[t_idx, k_idx].to(out.dtype)[:, None]
         out.index_add_(0, t_idx, y * wk)
     return out.to(torch.float32)
+
+def shared_expert_forward(x: torch.Tensor, w13_s: torch.Tensor, w2_s: torch.Tensor,
+                          gate_s: torch.Tensor | None) -> torch.Tensor:
+    """Drama-3's shared expert on the CPU, fp32: bf16 w13_s [2I, H] (gate rows
+    [0, I), up rows [I, 2I)), w2_s [H, I]; out = sigmoid(x . gate_s) *
+    (silu(x W_g^T) * (x W_u^T)) W_d^T, ungated when gate_s is None.  The
+    upstream block runs it beside the routed experts for every token
+    (notes/01-static-findings.md:80-82; ``shared_expert_gate: true`` and
+    ``shared_expert_intermediate_size: 512``, notes/drama3-config.json:215-216;
+    the sigmoid gate follows the usual shared-expert gating and is inferred).
+    Returns float32 [T, H]."""
+    I = w13_s.shape[0] // 2
+    xf = x.float()
+    gu = xf @ w13_s.float().T
+    h = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    y = h @ w2_s.float().T
+    if gate_s is not None:
+        y = y * torch.sigmoid(xf @ gate_s.float().reshape(-1))[:, None]
+    return y

@@ -67,6 +67,11 @@ def test_argument_validation_without_gpu():
     d.policy = 1  # LFU without freq/ins tables
     d.bytes[0] = 48
     assert lib.d3_resolve_fetch(ctypes.byref(d), z, 4, 8, 0, P(0)) == -1
+    # census / trace: null pointers, id width, a call larger than the ring
+    assert lib.d3_census_add(P(0), 4, 1, 8, 256, z, z, P(0)) == -1
+    assert lib.d3_census_add(z, 2, 1, 8, 256, z, z, P(0)) == -1
+    assert lib.d3_trace_append(z, 4, 10, 8, 0, z, z, 4, P(0)) == -6
+    assert lib.d3_trace_append(z, 4, 1, 8, 0, P(0), z, 4, P(0)) == -1
 
 
 def test_layer_cache_struct_layout():

@@ -282,3 +282,52 @@ def test_moe_forward_deterministic_with_fresh_inputs(E, T, k):
     moe.check_errors(DEV)
     assert all(torch.equal(outs[0], o) for o in outs[1:])
     assert torch.isfinite(outs[0].float()).all()
+
+
+def _shared(H=2048, I=512, seed=3, gated=True):
+    g = torch.Generator().manual_seed(seed)
+    sw13 = (torch.randn(2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    sw2 = (torch.randn(H, I, generator=g) * 0.02).to(torch.bfloat16)
+    sg = (torch.randn(H, generator=g) * 0.02).to(torch.bfloat16) if gated else None
+    return sw13, sw2, sg
+
+
+@pytest.mark.parametrize("T,gated,acc", [(1, True, False), (2, True, True), (4, False, False),
+                                         (16, True, False), (16, True, True)])
+def test_moe_forward_with_shared_expert(T, gated, acc):
+    """Routed experts + Drama-3's gated shared expert: fused into the two
+    decode launches (T * 8 <= 32), two plain bf16 GEMMs beside the routed
+    path above that; both against the oracle."""
+    ex, x, ids, w = _rand_case(64, T, 8, 60 + T)
+    sw13, sw2, sg = _shared(gated=gated)
+    xd = x.to(DEV)
+    out = xd.clone() if acc else None
+    shared = (sw13.to(DEV), sw2.to(DEV), sg.to(DEV) if sg is not None else None)
+    got = moe.fp8_moe_forward(xd, ids.to(DEV), w.to(DEV), ex.w13_weight, ex.w13_scale_inv,
+                              ex.w2_weight, ex.w2_scale_inv, out=out, accumulate=acc,
+                              shared=shared)
+    moe.check_errors(DEV)
+    cpu = ex.to("cpu")
+    ref = oracle.moe_forward(x, ids, w, cpu.w13_weight, cpu.w13_scale_inv, cpu.w2_weight,
+                             cpu.w2_scale_inv)
+    ref = ref + oracle.shared_expert_forward(x, sw13, sw2, sg)
+    if acc:
+        ref = ref + x.float()
+    assert rel_err(got, ref) < TOL, rel_err(got, ref)
+
+
+def test_shared_expert_fused_entry_rejects_large_batch():
+    from drama3_offloading_b200 import _lib
+    ex, x, ids, w = _rand_case(16, 8, 8, 70)     # 64 pairs: not a decode batch
+    sw13, sw2, sg = [t.to(DEV) for t in _shared(seed=4)]
+    xd, idd, wd = x.to(DEV), ids.to(DEV), w.to(DEV)
+    out = torch.empty_like(xd)
+    need = moe.workspace_bytes(8, 8, 16, 2048, 512)
+    ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+    P = _lib.ptr
+    with pytest.raises(_lib.D3Error) as ei:
+        _lib.call("d3_moe_fp8_forward_shared", P(xd), P(idd), 4, P(wd), 1, 8, 8,
+                  P(ex.w13_weight), P(ex.w13_scale_inv), P(ex.w2_weight), P(ex.w2_scale_inv),
+                  16, 2048, 512, P(sw13), P(sw2), P(sg), P(out), 0, P(moe.error_word(DEV)),
+                  P(ws), ws.numel(), _lib.stream_ptr())
+    assert ei.value.status == -5   # D3_ERR_UNSUPPORTED
