@@ -95,7 +95,7 @@ class CpuDecodeSample:
     into a host-side cache, and the oracle's dequantise-then-matmul experts
     (the reference's torch CPU MoE path).  A bounded sample of the 40 layers."""
 
-    def __init__(self, layers, trace, capacity, hidden=2048, inter=512, experts=256, R=22528,
+    def __init__(self, layers, trace, capacity, hidden=2048, inter=512, experts=256, R=None,
                  seed=0):
         import oracle
         from drama3_offloading_b200 import synth
@@ -105,6 +105,10 @@ class CpuDecodeSample:
         gen = "cuda" if torch.cuda.is_available() else "cpu"
         g = torch.Generator().manual_seed(seed + 7)
         self.L, self.k, self.trace = layers, trace.shape[2], trace
+        if R is None:  # the GPU stack's dense stand-in rows (6.9 GiB with the shared experts)
+            from drama3_offloading_b200.decode import DENSE_GIB
+            per = DENSE_GIB * (1 << 30) / 40 - (3 * inter * hidden + hidden) * 2
+            R = max(128, int(per / (2 * hidden * 2)) // 128 * 128)
         self.ex = [synth.make_experts(experts, hidden, inter, seed=seed + l, device=gen,
                                       chunk=32).to("cpu") for l in range(layers)]
         self.up = [(torch.randn(R, hidden, generator=g) * hidden ** -0.5).to(torch.bfloat16)
@@ -113,6 +117,10 @@ class CpuDecodeSample:
                      for _ in range(layers)]
         self.gate = [(torch.randn(experts, hidden, generator=g) * 0.02).to(torch.bfloat16)
                      for _ in range(layers)]
+        self.shared = [((torch.randn(2 * inter, hidden, generator=g) * 0.02).to(torch.bfloat16),
+                        (torch.randn(hidden, inter, generator=g) * 0.02).to(torch.bfloat16),
+                        (torch.randn(hidden, generator=g) * 0.02).to(torch.bfloat16))
+                       for _ in range(layers)]
         self.tabs = [oracle.init_tables(experts, capacity) for _ in range(layers)]
         self.c13 = [torch.zeros((capacity, 2 * inter, hidden), dtype=torch.float8_e4m3fn)
                     for _ in range(layers)]
@@ -131,6 +139,7 @@ class CpuDecodeSample:
             h = self.h
             h = h + torch.nn.functional.silu(h @ self.up[l].t()) @ self.down[l].t()
             _, w, _, _ = o.router_topk(h, self.gate[l], self.k)
+            ys = o.shared_expert_forward(h, *self.shared[l])
             slots, fs, fe, n = o.resolve(self.tabs[l], row[l])
             ex = self.ex[l]
             for j in range(n):
@@ -141,7 +150,7 @@ class CpuDecodeSample:
                 self.s2[l][s].copy_(ex.w2_scale_inv[e])
             y = o.moe_forward(h, torch.from_numpy(slots.astype(np.int64)).reshape(1, -1), w,
                               self.c13[l], self.s13[l], self.c2[l], self.s2[l])
-            y = h.float() + y
+            y = h.float() + y + ys
             y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6)
             self.h = y.to(torch.bfloat16)
         self.pos += 1
@@ -160,7 +169,8 @@ def cpu_decode_baseline(trace, capacity, layers_total, sample_layers, sample_s) 
             "kind": "port",
             "sample": f"{len(times)} tokens x {sample_layers} of {layers_total} layers (per-token "
                       f"time scaled by {layers_total}/{sample_layers}); torch bf16 dense GEMVs + "
-                      f"oracle router/LRU + expert memcpy + dequantised fp32 expert matmuls"}
+                      f"oracle router/LRU + expert memcpy + dequantised fp32 expert matmuls + "
+                      f"shared expert"}
 
 
 def cpu_fetch_baseline(trace, capacity, sample_s) -> dict:
@@ -755,7 +765,8 @@ def main():
                 "dtype": "fp8 weights x bf16 activations (fp32 accumulate), bf16 dense",
                 "data": "synthetic (random-init Drama-3 shapes, seeded Zipf(1.1) routing trace)",
                 "config": {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
-                           "hidden": 2048, "experts": 256, "topk": 8, "cache_gib": args.cache_gib,
+                           "hidden": 2048, "experts": 256, "topk": 8, "shared_expert": True,
+                           "cache_gib": args.cache_gib,
                            "slots_per_layer": r["capacity"], "policy": args.policy,
                            "dense_gib_per_token": r["dense_bytes"] / 2**30,
                            "l2": "inputs > L2 (30 GiB host store, 6.9 GiB dense, 8 GiB cache)",

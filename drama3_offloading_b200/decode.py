@@ -6,13 +6,15 @@ random-initialised at the real shapes.
 Per layer and decode token (batch 1):
 
 1. dense stand-in: ``h += down(silu(up(h)))`` with bf16 weights sized so the
-   40 layers read 6.9 GiB per token -- the non-expert (attention / GDN /
-   shared-expert / projection) weight traffic of Drama-3 (notes/01-static-
-   findings.md:54-55).  Plain cuBLAS GEMVs: not part of the hot path.
+   40 layers read 6.9 GiB per token together with the shared experts -- the
+   non-routed (attention / GDN / shared-expert / projection) weight traffic
+   of Drama-3 (notes/01-static-findings.md:54-55, :80-82).  Plain cuBLAS
+   GEMVs: not part of the hot path.
 2. router ``d3_router_topk`` on the layer's bf16 gate [256, 2048].
 3. ``d3_resolve_fetch``: device slot allocator + fetch of the missed experts
    from pinned host memory into the layer's device cache.
-4. ``d3_moe_fp8_forward`` on the cache slots, accumulated into ``h``.
+4. ``d3_moe_fp8_forward_shared`` on the cache slots plus the layer's gated
+   bf16 shared expert (resident, 6 MiB), accumulated into ``h``.
 
 Routing: the router runs every layer (its cost is real), but the expert ids
 fed to the cache come from the seeded Zipf(1.1) trace so hit rates are those
@@ -47,15 +49,25 @@ class DecodeStack:
                                       policy, fill, group=group, local_rank=local_rank)
         self.trace_offset = trace_offset
         g = torch.Generator(device=dev).manual_seed(seed + 7)
+        # the shared expert of every layer (bf16 gate/up [2I, H], down [H, I],
+        # sigmoid gate [H]), resident; its bytes come out of the dense budget
+        self.shared = [((torch.randn(2 * inter, hidden, generator=g, device=dev) * 0.02)
+                        .to(torch.bfloat16),
+                        (torch.randn(hidden, inter, generator=g, device=dev) * 0.02)
+                        .to(torch.bfloat16),
+                        (torch.randn(hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+                       for _ in range(layers)]
+        shared_bytes = (3 * inter * hidden + hidden) * 2
         # dense stand-in: 2 * R * H bf16 per layer
-        per_layer = dense_gib * (1 << 30) / layers
+        per_layer = dense_gib * (1 << 30) / layers - shared_bytes
         R = max(128, int(per_layer / (2 * hidden * 2)) // 128 * 128)
         self.R = R
         self.up = [torch.randn(R, hidden, generator=g, device=dev, dtype=torch.bfloat16) * (hidden ** -0.5)
                    for _ in range(layers)]
         self.down = [torch.randn(hidden, R, generator=g, device=dev, dtype=torch.bfloat16) * (R ** -0.5 * 0.5)
                      for _ in range(layers)]
-        self.dense_bytes = sum(t.numel() * 2 for t in self.up + self.down)
+        self.dense_bytes = (sum(t.numel() * 2 for t in self.up + self.down) +
+                            layers * shared_bytes)
         self.gate = [(torch.randn(experts, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
                      for _ in range(layers)]
         self.h = torch.zeros(1, hidden, dtype=torch.bfloat16, device=dev)
@@ -89,7 +101,8 @@ class DecodeStack:
             e1.record()
             events.append((e0, e1))
         moe.fp8_moe_forward(h, slots.reshape(1, self.k), self.wts, ex._dc_w13, ex._dc_s13,
-                            ex._dc_w2, ex._dc_s2, out=h, accumulate=True)
+                            ex._dc_w2, ex._dc_s2, out=h, accumulate=True,
+                            shared=self.shared[l])
 
     def step(self) -> None:
         """One decode token through all layers (eager; capturable)."""
