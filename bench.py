@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--ep-exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="ep workload: NVLink peer stores or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -592,8 +594,9 @@ def run_layer(args, rank, world, local):
 def run_ep(args, rank, world, local):
     """Fully resident expert-parallel decode: 256 experts sharded 256/N per
     GPU, global batch 64 split over the ranks, uniform-random top-8 routing,
-    NCCL all-to-all dispatch/combine, 40 layers per step in one CUDA graph."""
-    from drama3_offloading_b200 import benchutil
+    dispatch/combine over NVLink peer stores (or NCCL all-to-all with
+    --ep-exchange nccl), 40 layers per step in one CUDA graph."""
+    from drama3_offloading_b200 import benchutil, moe
     from drama3_offloading_b200.ep import ExpertParallelMoE, synth_expert_bytes
     from drama3_offloading_b200.trace import uniform_trace
 
@@ -601,7 +604,8 @@ def run_ep(args, rank, world, local):
     torch.cuda.set_device(dev)
     trace = uniform_trace(steps=256, tokens=args.global_batch, layers=args.layers)
     m = ExpertParallelMoE(layers=args.layers, global_batch=args.global_batch, rank=rank,
-                          world=world, group=local_group(world), device=dev, trace=trace)
+                          world=world, group=local_group(world), device=dev, trace=trace,
+                          exchange=args.ep_exchange)
     g = m.capture()
     m.step_idx.zero_()
     for _ in range(args.warmup):
@@ -649,7 +653,13 @@ def run_ep(args, rank, world, local):
     else:
         gbs_all = [gemm_gbs]
     overflow = int(m.overflow.item())
+    moe.check_errors(dev)   # a bounded exchange wait that ran out would show here
+    g = None
+    m.close()
     value = args.global_batch * args.steps / (ms * 1e-3)
+    exch = {"p2p": "NVLink peer stores + epoch flags (CUDA IPC), static capacity",
+            "nccl": "NCCL all-to-all, static capacity", "none": "none"}[m.exchange]
+    per_layer = {"p2p": 13, "nccl": 10, "none": 7}[m.exchange]
     return {
         "metric": "resident expert-parallel decode tok/s (40L, batch 64, 256 experts / N GPUs)",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -659,7 +669,7 @@ def run_ep(args, rank, world, local):
         "data": "synthetic (random-init FP8 experts, uniform-random top-8 routing)",
         "config": {"workload": "ep-resident-decode", "layers": args.layers, "experts": 256,
                    "experts_per_gpu": m.epr, "global_batch": args.global_batch, "topk": 8,
-                   "parallelism": f"ep{world}", "exchange": "NCCL all-to-all, static capacity",
+                   "parallelism": f"ep{world}", "exchange": exch,
                    "l2": f"inputs > L2 ({args.layers * m.epr * eb / 2**30:.1f} GiB resident "
                          f"experts per GPU)"},
         "roofline": {"bound": "hbm", "kernel": "expert GEMMs (d3_moe_fp8_forward, per rank)",
@@ -668,7 +678,7 @@ def run_ep(args, rank, world, local):
                      "bytes": "distinct local experts x 3,146,496 B per layer",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "overflow_pairs": overflow, "clocks": clk.summary(),
-        "gpu_launches": args.steps * args.layers * (7 if world == 1 else 10),
+        "gpu_launches": args.steps * args.layers * per_layer,
     }
 
 

@@ -67,6 +67,13 @@ SIGNATURES: dict[str, tuple] = {
     "d3_gather_experts": (ctypes.c_int, [ctypes.POINTER(LayerCache), P, P, P, P, I32, P]),
     "d3_ep_dispatch_pack":(ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P]),
     "d3_ep_combine": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, I32, P]),
+    "d3_ipc_get": (ctypes.c_int, [P, P, P]),
+    "d3_ipc_open": (ctypes.c_int, [P, P]),
+    "d3_ipc_close": (ctypes.c_int, [P]),
+    "d3_ep_dispatch_p2p": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P, P, P,
+                                          P, P, P]),
+    "d3_ep_return_p2p": (ctypes.c_int, [P, P, I32, I32, I32, I32, P, P, P, P, P]),
+    "d3_ep_wait": (ctypes.c_int, [P, I32, P, P, I32, I64, P]),
     "d3_census_add": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, P]),
     "d3_trace_append": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, I64, P]),
 }

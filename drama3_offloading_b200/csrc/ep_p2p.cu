@@ -1,0 +1,317 @@
+// Expert-parallel exchange over NVLink peer memory (no NCCL on the data path).
+//
+// Every rank owns one exchange buffer in its own HBM, mapped into every other
+// rank's process through CUDA IPC; all ranks use the same layout:
+//   recv_x   [n_ranks * cap, H] bf16   rows sent TO this rank, block per source rank
+//   recv_eid [n_ranks * cap] int32    local expert id of each row (-1: unused)
+//   ret      [n_ranks * cap, H] bf16   expert outputs sent back TO this rank,
+//                                      block per serving rank
+//   flag_d   [n_ranks] int64          dispatch epoch written by each source rank
+//   flag_r   [n_ranks] int64          return epoch written by each serving rank
+// (the same row layout the NCCL all-to-all path produces, so the expert call
+// and d3_ep_combine are shared).
+//
+// Per layer: d3_ep_dispatch_p2p (plan: stable per-destination ranks, eids
+// written straight into the destinations' recv_eid; copy: token rows stored
+// straight into the destinations' recv_x; the last CTA publishes
+// flag_d[rank] = epoch on every destination with a system-scope release) ->
+// d3_ep_wait on the local flag_d -> the expert call on recv_x ->
+// d3_ep_return_p2p (each served row stored into its source's ret, flag_r) ->
+// d3_ep_wait on flag_r -> d3_ep_combine.  The epoch is a device counter the
+// plan launch increments once per layer, so every rank agrees on it without a
+// host round trip and the whole step stays graph-capturable.
+//
+// Waits spin on system-scope acquire loads with a %globaltimer budget; on
+// expiry the kernel records an error code and returns.  Plain peer stores
+// only: no multicast objects, no TMA on peer memory.
+//
+// No counterpart in the reference (it has no multi-GPU code).
+#include "d3_common.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+namespace d3 {
+
+constexpr int kP2pMaxRanks = 16;
+
+struct P2pDispatchParams {
+  const int32_t* ids;
+  int T, topk, n_ranks, rank, epr, cap;
+  int32_t* recv_eid[kP2pMaxRanks];      // each destination's recv_eid
+  __nv_bfloat16* recv_x[kP2pMaxRanks];  // each destination's recv_x
+  long long* flag_d[kP2pMaxRanks];      // each destination's flag_d
+  int32_t* src_slot;                    // [T * topk] local
+  int32_t* overflow;
+  long long* epoch;                     // local device epoch
+  unsigned int* counter;                // local, zero between launches
+  const __nv_bfloat16* x;               // [T, H]
+  int H;
+};
+
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One CTA: the layer's epoch, stable ranks per destination (pair order), the
+// destinations' recv_eid rows of this source block (unused rows -1).
+__global__ void __launch_bounds__(256) p2p_plan_kernel(P2pDispatchParams p) {
+  __shared__ int cursor[kP2pMaxRanks];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid == 0) *p.epoch += 1;
+  for (int d = tid; d < p.n_ranks; d += blockDim.x) cursor[d] = 0;
+  __syncthreads();
+  const int P = p.T * p.topk;
+  if (tid < 32) {
+    for (int b0 = 0; b0 < P; b0 += 32) {
+      const int i = b0 + lane;
+      const int e = i < P ? p.ids[i] : -1;
+      const int d = (e >= 0 && e < p.n_ranks * p.epr) ? e / p.epr : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, d);
+      const int leader = __ffs(m) - 1;
+      int base = 0;
+      if (lane == leader && d >= 0) {
+        base = cursor[d];
+        cursor[d] = base + __popc(m);
+      }
+      base = __shfl_sync(0xffffffffu, base, leader);
+      if (i < P) {
+        int slot = -1;
+        if (d >= 0) {
+          const int j = base + __popc(m & ((1u << lane) - 1));
+          if (j < p.cap) {
+            slot = d * p.cap + j;
+            p.recv_eid[d][p.rank * p.cap + j] = e - d * p.epr;
+          } else {
+            atomicAdd(p.overflow, 1);
+          }
+        }
+        p.src_slot[i] = slot;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int d = 0; d < p.n_ranks; ++d)
+    for (int j = cursor[d] + tid; j < p.cap; j += blockDim.x)
+      p.recv_eid[d][p.rank * p.cap + j] = -1;
+  __threadfence_system();  // the peer eid stores before anything this rank signals later
+}
+
+// One CTA per pair: its token row into the destination's recv_x; the last CTA
+// to finish publishes the epoch on every destination.
+__global__ void __launch_bounds__(128) p2p_copy_kernel(P2pDispatchParams p) {
+  __shared__ bool s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x;
+  const int slot = p.src_slot[i];
+  if (slot >= 0) {
+    const int d = slot / p.cap, j = slot - d * p.cap;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)(i / p.topk) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(p.recv_x[d] + (size_t)(p.rank * p.cap + j) * p.H);
+    for (int v = threadIdx.x; v < p.H / 8; v += blockDim.x) dst[v] = src[v];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();  // every CTA's peer stores (fenced before its arrival) come first
+  if (threadIdx.x < p.n_ranks) st_release_sys(p.flag_d[threadIdx.x] + p.rank, *p.epoch);
+  if (threadIdx.x == 0) *p.counter = 0;
+}
+
+struct P2pReturnParams {
+  const __nv_bfloat16* y;               // [n_ranks * cap, H] local expert outputs
+  const int32_t* recv_eid;              // local
+  int n_ranks, rank, cap, H;
+  __nv_bfloat16* ret[kP2pMaxRanks];     // each source's ret
+  long long* flag_r[kP2pMaxRanks];      // each source's flag_r
+  const long long* epoch;
+  unsigned int* counter;
+};
+
+// One CTA per received row: served rows back to their source rank.
+__global__ void __launch_bounds__(128) p2p_return_kernel(P2pReturnParams p) {
+  __shared__ bool s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  if (p.recv_eid[row] >= 0) {
+    const int s = row / p.cap, j = row - s * p.cap;
+    const uint4* src = reinterpret_cast<const uint4*>(p.y + (size_t)row * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(p.ret[s] + (size_t)(p.rank * p.cap + j) * p.H);
+    for (int v = threadIdx.x; v < p.H / 8; v += blockDim.x) dst[v] = src[v];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  if (threadIdx.x < p.n_ranks) st_release_sys(p.flag_r[threadIdx.x] + p.rank, *p.epoch);
+  if (threadIdx.x == 0) *p.counter = 0;
+}
+
+// One warp: lane r waits (bounded) until flags[r] >= *epoch.
+__global__ void p2p_wait_kernel(const long long* flags, int n_ranks, const long long* epoch,
+                                int* err, int code, unsigned long long budget_ns) {
+  pdl_wait();
+  const int lane = threadIdx.x;
+  bool ok = true;
+  if (lane < n_ranks) {
+    const long long want = *epoch;
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_sys(flags + lane) < want) {
+      if (globaltimer_ns() - t0 > budget_ns) { ok = false; break; }
+      __nanosleep(64);
+    }
+  }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) atomicCAS(err, 0, code);
+  __syncwarp();
+  pdl_trigger();
+}
+
+// ---- IPC: the owning allocation of a device pointer, shared across processes
+
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(f);
+  });
+  return fn;
+}
+
+}  // namespace d3
+
+using namespace d3;
+
+extern "C" {
+
+int d3_ipc_get(const void* ptr, void* handle, uint64_t* offset) {
+  D3_CHECK_ARG(ptr && handle && offset, "d3_ipc_get: null pointer");
+  GetAddressRangeFn fn = address_range_fn();
+  if (!fn) return fail(D3_ERR_CUDA, "cuMemGetAddressRange unavailable from the driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(D3_ERR_CUDA, "cuMemGetAddressRange failed (%d)", (int)r);
+  cudaIpcMemHandle_t h;
+  D3_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<uint64_t>(ptr) - (uint64_t)base;
+  return D3_OK;
+}
+
+int d3_ipc_open(const void* handle, void** base) {
+  D3_CHECK_ARG(handle && base, "d3_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  D3_CUDA_TRY(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess),
+              "cudaIpcOpenMemHandle");
+  return D3_OK;
+}
+
+int d3_ipc_close(void* base) {
+  D3_CHECK_ARG(base, "d3_ipc_close: null pointer");
+  D3_CUDA_TRY(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+  return D3_OK;
+}
+
+int d3_ep_dispatch_p2p(const void* x, const int32_t* ids, int32_t T, int32_t topk, int32_t H,
+                       int32_t n_ranks, int32_t rank, int32_t experts_per_rank, int32_t cap,
+                       void* const* peer_recv_x, int32_t* const* peer_recv_eid,
+                       int64_t* const* peer_flag_d, int32_t* src_slot, int32_t* overflow,
+                       int64_t* epoch, uint32_t* counter, d3_stream_t stream) {
+  D3_CHECK_ARG(x && ids && peer_recv_x && peer_recv_eid && peer_flag_d && src_slot && overflow &&
+                   epoch && counter,
+               "d3_ep_dispatch_p2p: null pointer");
+  D3_CHECK_ARG(T >= 1 && topk >= 1 && topk <= 64 && (long)T * topk <= 65536,
+               "T, topk out of range");
+  D3_CHECK_ARG(H >= 8 && H % 8 == 0, "H must be a positive multiple of 8");
+  if (n_ranks < 1 || n_ranks > kP2pMaxRanks)
+    return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, %d]", kP2pMaxRanks);
+  D3_CHECK_ARG(rank >= 0 && rank < n_ranks && experts_per_rank >= 1 && cap >= 1,
+               "rank, experts_per_rank, cap out of range");
+  if (!aligned16(x)) return fail(D3_ERR_MISALIGNED, "x must be 16-byte aligned");
+  P2pDispatchParams p{};
+  p.ids = ids; p.T = T; p.topk = topk; p.n_ranks = n_ranks; p.rank = rank;
+  p.epr = experts_per_rank; p.cap = cap; p.src_slot = src_slot; p.overflow = overflow;
+  p.epoch = reinterpret_cast<long long*>(epoch); p.counter = counter;
+  p.x = static_cast<const __nv_bfloat16*>(x); p.H = H;
+  for (int d = 0; d < n_ranks; ++d) {
+    D3_CHECK_ARG(peer_recv_x[d] && peer_recv_eid[d] && peer_flag_d[d],
+                 "d3_ep_dispatch_p2p: null peer pointer");
+    if (!aligned16(peer_recv_x[d]))
+      return fail(D3_ERR_MISALIGNED, "peer recv_x must be 16-byte aligned");
+    p.recv_x[d] = static_cast<__nv_bfloat16*>(peer_recv_x[d]);
+    p.recv_eid[d] = peer_recv_eid[d];
+    p.flag_d[d] = reinterpret_cast<long long*>(peer_flag_d[d]);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  // first launch of the call: an ordinary stream dependent
+  D3_CUDA_TRY(launch_k(p2p_plan_kernel, dim3(1), dim3(256), 0, st, false, p), "p2p_plan_kernel");
+  D3_CUDA_TRY(launch_k(p2p_copy_kernel, dim3((unsigned)(T * topk)), dim3(128), 0, st,
+                       pdl_enabled(), p),
+              "p2p_copy_kernel");
+  return D3_OK;
+}
+
+int d3_ep_return_p2p(const void* y, const int32_t* recv_eid, int32_t n_ranks, int32_t rank,
+                     int32_t cap, int32_t H, void* const* peer_ret, int64_t* const* peer_flag_r,
+                     const int64_t* epoch, uint32_t* counter, d3_stream_t stream) {
+  D3_CHECK_ARG(y && recv_eid && peer_ret && peer_flag_r && epoch && counter,
+               "d3_ep_return_p2p: null pointer");
+  D3_CHECK_ARG(H >= 8 && H % 8 == 0 && cap >= 1, "bad shape");
+  if (n_ranks < 1 || n_ranks > kP2pMaxRanks)
+    return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, %d]", kP2pMaxRanks);
+  D3_CHECK_ARG(rank >= 0 && rank < n_ranks, "rank out of range");
+  if (!aligned16(y)) return fail(D3_ERR_MISALIGNED, "y must be 16-byte aligned");
+  P2pReturnParams p{};
+  p.y = static_cast<const __nv_bfloat16*>(y); p.recv_eid = recv_eid;
+  p.n_ranks = n_ranks; p.rank = rank; p.cap = cap; p.H = H;
+  p.epoch = reinterpret_cast<const long long*>(epoch); p.counter = counter;
+  for (int s = 0; s < n_ranks; ++s) {
+    D3_CHECK_ARG(peer_ret[s] && peer_flag_r[s], "d3_ep_return_p2p: null peer pointer");
+    if (!aligned16(peer_ret[s])) return fail(D3_ERR_MISALIGNED, "peer ret must be 16-byte aligned");
+    p.ret[s] = static_cast<__nv_bfloat16*>(peer_ret[s]);
+    p.flag_r[s] = reinterpret_cast<long long*>(peer_flag_r[s]);
+  }
+  D3_CUDA_TRY(launch_k(p2p_return_kernel, dim3((unsigned)(n_ranks * cap)), dim3(128), 0,
+                       (cudaStream_t)stream, false, p),
+              "p2p_return_kernel");
+  return D3_OK;
+}
+
+int d3_ep_wait(const int64_t* flags, int32_t n_ranks, const int64_t* epoch, int32_t* err_word,
+               int32_t code, int64_t budget_ns, d3_stream_t stream) {
+  D3_CHECK_ARG(flags && epoch && err_word, "d3_ep_wait: null pointer");
+  if (n_ranks < 1 || n_ranks > 32) return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, 32]");
+  D3_CHECK_ARG(budget_ns > 0, "budget_ns must be positive");
+  D3_CUDA_TRY(launch_k(p2p_wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, false,
+                       reinterpret_cast<const long long*>(flags), (int)n_ranks,
+                       reinterpret_cast<const long long*>(epoch), err_word, (int)code,
+                       (unsigned long long)budget_ns),
+              "p2p_wait_kernel");
+  return D3_OK;
+}
+
+}  // extern "C"

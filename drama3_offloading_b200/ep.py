@@ -4,11 +4,16 @@
 N = 8) and stay resident in HBM; the global decode batch (64 streams) is
 split over the ranks (64/N tokens each).  Per layer and step, on every rank:
 
-    router (local tokens) -> d3_ep_dispatch_pack (static capacity per peer)
-    -> NCCL all-to-all of the token rows + local expert ids
-    -> d3_moe_fp8_forward over the received rows (one expert per row)
-    -> NCCL all-to-all of the expert outputs back
+    router (local tokens) -> d3_ep_dispatch_p2p: token rows and local expert
+    ids stored straight into the destination ranks' exchange buffers over
+    NVLink (static capacity per peer), epoch flag released on each
+    -> d3_ep_wait (all sources arrived) -> d3_moe_fp8_forward over the
+    received rows (one expert per row) -> d3_ep_return_p2p: outputs stored
+    back into the source ranks' buffers -> d3_ep_wait
     -> d3_ep_combine: h += sum_k w[t,k] y[t,k]
+
+``exchange="nccl"`` runs the same step with NCCL all-to-alls instead (pack
+locally, all-to-all rows and ids, all-to-all outputs back).
 
 Every buffer has a fixed shape (capacity = local pairs per peer), so the step
 needs no host sync and is captured into one CUDA graph, collectives included.
@@ -17,6 +22,8 @@ At N = 1 the exchange disappears and the layer is one fp8_moe_forward.
 No counterpart in the reference (it has no multi-GPU code).
 """
 from __future__ import annotations
+
+import ctypes
 
 import numpy as np
 import torch
@@ -31,11 +38,67 @@ def exchange(send: torch.Tensor, recv: torch.Tensor, group=None) -> None:
     dist.all_to_all_single(recv, send, group=group)
 
 
+def _al(v: int) -> int:
+    return (v + 255) // 256 * 256
+
+
+class P2PExchange:
+    """Every rank's exchange buffer (recv_x, recv_eid, ret, flag_d, flag_r;
+    layout of csrc/ep_p2p.cu) in its own HBM, mapped into every rank's
+    process through CUDA IPC, and the per-peer device pointers the kernels
+    store into.  The handles travel once over the process group at setup."""
+
+    def __init__(self, rank: int, world: int, cap: int, H: int, device, group=None):
+        import torch.distributed as dist
+        if world > 16:
+            raise ValueError("the NVLink exchange takes at most 16 ranks")
+        self.rank, self.world = rank, world
+        n = world * cap
+        self.off = {}
+        o = 0
+        for name, nbytes in (("recv_x", n * H * 2), ("recv_eid", n * 4), ("ret", n * H * 2),
+                             ("flag_d", world * 8), ("flag_r", world * 8)):
+            self.off[name] = o
+            o += _al(nbytes)
+        self.buf = torch.zeros(o, dtype=torch.uint8, device=device)
+        view = lambda name, nbytes, dt: self.buf[self.off[name]:self.off[name] + nbytes].view(dt)
+        self.recv_x = view("recv_x", n * H * 2, torch.bfloat16).view(n, H)
+        self.recv_eid = view("recv_eid", n * 4, torch.int32)
+        self.ret = view("ret", n * H * 2, torch.bfloat16).view(n, H)
+        self.flag_d = view("flag_d", world * 8, torch.int64)
+        self.flag_r = view("flag_r", world * 8, torch.int64)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=device)
+        self.counters = torch.zeros(2, dtype=torch.int32, device=device)
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_uint64()
+        _lib.call("d3_ipc_get", _lib.ptr(self.buf), handle, ctypes.byref(offset))
+        infos = [None] * world
+        dist.all_gather_object(infos, (bytes(handle), offset.value), group=group)
+        self.opened = []
+        bases = []
+        for r, (h, off) in enumerate(infos):
+            if r == rank:
+                bases.append(self.buf.data_ptr())
+                continue
+            b = ctypes.c_void_p()
+            _lib.call("d3_ipc_open", ctypes.create_string_buffer(h, 64), ctypes.byref(b))
+            self.opened.append(b.value)
+            bases.append(b.value + off)
+        arr = lambda name: (ctypes.c_void_p * world)(*(b + self.off[name] for b in bases))
+        self.peer = {name: arr(name) for name in self.off}
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        for b in self.opened:
+            _lib.call("d3_ipc_close", ctypes.c_void_p(b))
+        self.opened = []
+
+
 class ExpertParallelMoE:
     def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048,
                  inter: int = 512, topk: int = 8, global_batch: int = 64, rank: int = 0,
                  world: int = 1, group=None, device="cuda", seed: int = 0,
-                 trace: np.ndarray | None = None):
+                 trace: np.ndarray | None = None, exchange: str = "p2p"):
         if experts % world or global_batch % world:
             raise ValueError("experts and global_batch must divide evenly over the ranks")
         self.device = dev = torch.device(device)
@@ -63,6 +126,11 @@ class ExpertParallelMoE:
         self.src_slot = torch.full((self.T, topk), -1, dtype=torch.int32, device=dev)
         self.ones = torch.ones(n, 1, dtype=torch.float32, device=dev)
         self.overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        self.exchange = exchange if world > 1 else "none"
+        self.p2p = P2PExchange(rank, world, self.cap, hidden, dev, group) \
+            if self.exchange == "p2p" else None
         if trace is None:
             from .trace import uniform_trace
             trace = uniform_trace(steps=256, tokens=global_batch, layers=layers,
@@ -91,6 +159,9 @@ class ExpertParallelMoE:
                 gemm_events.append((e0, e1))
             return
         st = _lib.stream_ptr()
+        if self.p2p is not None:
+            self._layer_p2p(l, ids, w, st, gemm_events)
+            return
         _lib.call("d3_ep_dispatch_pack", _lib.ptr(h), _lib.ptr(ids), self.T, self.k, self.H,
                   self.world, self.epr, self.cap, _lib.ptr(self.send_x), _lib.ptr(self.send_eid),
                   _lib.ptr(self.src_slot), _lib.ptr(self.overflow), st)
@@ -107,6 +178,44 @@ class ExpertParallelMoE:
         exchange(self.y, self.ret, self.group)
         _lib.call("d3_ep_combine", _lib.ptr(self.ret), _lib.ptr(self.src_slot),
                   _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(h), 1, st)
+
+    WAIT_BUDGET_NS = 2_000_000_000
+
+    def _layer_p2p(self, l, ids, w, st, gemm_events) -> None:
+        """The same layer with the exchange over NVLink peer stores."""
+        x = self.p2p
+        err = moe.error_word(self.device)
+        _lib.call("d3_ep_dispatch_p2p", _lib.ptr(self.h), _lib.ptr(ids), self.T, self.k, self.H,
+                  self.world, self.rank, self.epr, self.cap, x.peer["recv_x"],
+                  x.peer["recv_eid"], x.peer["flag_d"], _lib.ptr(self.src_slot),
+                  _lib.ptr(self.overflow), _lib.ptr(x.epoch), _lib.ptr(x.counters), st)
+        _lib.call("d3_ep_wait", _lib.ptr(x.flag_d), self.world, _lib.ptr(x.epoch),
+                  _lib.ptr(err), 31, self.WAIT_BUDGET_NS, st)
+        if gemm_events is not None:
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+        moe.fp8_moe_forward(x.recv_x, x.recv_eid.view(-1, 1), self.ones, w.w13_weight,
+                            w.w13_scale_inv, w.w2_weight, w.w2_scale_inv, out=self.y)
+        if gemm_events is not None:
+            e1.record()
+            gemm_events.append((e0, e1))
+        _lib.call("d3_ep_return_p2p", _lib.ptr(self.y), _lib.ptr(x.recv_eid), self.world,
+                  self.rank, self.cap, self.H, x.peer["ret"], x.peer["flag_r"],
+                  _lib.ptr(x.epoch), _lib.ptr(x.counters[1:]), st)
+        _lib.call("d3_ep_wait", _lib.ptr(x.flag_r), self.world, _lib.ptr(x.epoch),
+                  _lib.ptr(err), 32, self.WAIT_BUDGET_NS, st)
+        _lib.call("d3_ep_combine", _lib.ptr(x.ret), _lib.ptr(self.src_slot),
+                  _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(self.h), 1, st)
+
+    def close(self) -> None:
+        """Unmap the peers' exchange buffers (after the last step, on every rank)."""
+        torch.cuda.synchronize(self.device)
+        self.graph = None
+        if self.p2p is not None:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+            self.p2p.close()
+            self.p2p = None
 
     def step(self, gemm_events: list | None = None) -> None:
         cur = self.trace_dev.index_select(0, self.step_idx)[0]

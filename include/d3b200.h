@@ -268,6 +268,43 @@ D3_API int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* w
                          int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
                          int32_t accumulate, d3_stream_t stream);
 
+/* ---------------------------------------------------------------- NVLink exchange (EP) */
+
+/* CUDA IPC of the allocation that holds `ptr`: a 64-byte handle plus ptr's
+ * offset inside it (d3_ipc_open in another process maps the allocation; add
+ * the offset).  For the expert-parallel exchange buffers. */
+D3_API int d3_ipc_get(const void* ptr, void* handle, uint64_t* offset);
+D3_API int d3_ipc_open(const void* handle, void** base);
+D3_API int d3_ipc_close(void* base);
+
+/* The expert-parallel dispatch over peer memory: the same packing as
+ * d3_ep_dispatch_pack, but each token row and local expert id is stored
+ * straight into its destination rank's exchange buffer (peer_recv_x[d],
+ * peer_recv_eid[d]: rows [rank*cap, (rank+1)*cap) belong to this source),
+ * then flag_d[rank] = epoch is released on every destination (*epoch is a
+ * device counter this call increments once).  counter: a device uint32 that
+ * is zero between calls.  n_ranks <= 16.  No counterpart in the reference. */
+D3_API int d3_ep_dispatch_p2p(const void* x, const int32_t* ids, int32_t T, int32_t topk,
+                              int32_t H, int32_t n_ranks, int32_t rank,
+                              int32_t experts_per_rank, int32_t cap, void* const* peer_recv_x,
+                              int32_t* const* peer_recv_eid, int64_t* const* peer_flag_d,
+                              int32_t* src_slot, int32_t* overflow, int64_t* epoch,
+                              uint32_t* counter, d3_stream_t stream);
+
+/* The return path: every received row with a valid expert id (recv_eid, local)
+ * goes from y (local expert outputs, [n_ranks*cap, H]) into its source rank's
+ * ret rows [rank*cap, ...), then flag_r[rank] = *epoch on every source. */
+D3_API int d3_ep_return_p2p(const void* y, const int32_t* recv_eid, int32_t n_ranks,
+                            int32_t rank, int32_t cap, int32_t H, void* const* peer_ret,
+                            int64_t* const* peer_flag_r, const int64_t* epoch, uint32_t* counter,
+                            d3_stream_t stream);
+
+/* One warp waits until flags[r] >= *epoch for every r < n_ranks (system-scope
+ * acquire loads), at most budget_ns of GPU time; on expiry *err_word = code
+ * (if it was 0) and the kernel returns. */
+D3_API int d3_ep_wait(const int64_t* flags, int32_t n_ranks, const int64_t* epoch,
+                      int32_t* err_word, int32_t code, int64_t budget_ns, d3_stream_t stream);
+
 /* ---------------------------------------------------------------- routing census / trace */
 
 /* counts[e] += occurrences of expert e among the rows*k ids (int32 or int64,

@@ -1,6 +1,7 @@
 """Expert-parallel dispatch/combine kernels on one GPU (n_ranks simulated)
 against the torch restatement, and -- when two GPUs are visible -- the
 2-rank NCCL expert-parallel layer against the single-GPU MoE forward."""
+import ctypes
 import os
 import socket
 import sys
@@ -57,6 +58,91 @@ def test_dispatch_pack_and_combine(n_ranks, T, k, cap):
     assert torch.allclose(out.float().cpu(), want, atol=2e-2, rtol=1e-2)
 
 
+def _p2p_buffers(n_ranks, cap, H):
+    n = n_ranks * cap
+    return {"recv_x": torch.zeros(n, H, dtype=torch.bfloat16, device=DEV),
+            "recv_eid": torch.full((n,), -7, dtype=torch.int32, device=DEV),
+            "ret": torch.zeros(n, H, dtype=torch.bfloat16, device=DEV),
+            "flag_d": torch.zeros(n_ranks, dtype=torch.int64, device=DEV),
+            "flag_r": torch.zeros(n_ranks, dtype=torch.int64, device=DEV),
+            "epoch": torch.zeros(1, dtype=torch.int64, device=DEV),
+            "ctr": torch.zeros(2, dtype=torch.int32, device=DEV)}
+
+
+@pytest.mark.parametrize("n_ranks,T", [(2, 4), (4, 2)])
+def test_p2p_exchange_emulated_ranks(n_ranks, T):
+    """The NVLink exchange kernels with every 'rank' on this GPU (peer pointers
+    are plain device pointers here): recv/ret buffers hold exactly the
+    all-to-all layout, the flags carry the epoch, waits return at once."""
+    E, H, k = 64, 2048, 8
+    epr, cap = E // n_ranks, T * k
+    g = torch.Generator().manual_seed(n_ranks * 10 + T)
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(n_ranks)]
+    ids = [torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+           for _ in range(n_ranks)]
+    bufs = [_p2p_buffers(n_ranks, cap, H) for _ in range(n_ranks)]
+    arr = lambda name: (ctypes.c_void_p * n_ranks)(*(_lib.ptr(b[name]).value for b in bufs))
+    srcs = [torch.zeros(T, k, dtype=torch.int32, device=DEV) for _ in range(n_ranks)]
+    ovf = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    keep = [(x.to(DEV), i.to(DEV)) for x, i in zip(xs, ids)]
+    st = _lib.stream_ptr()
+    for r in range(n_ranks):
+        _lib.call("d3_ep_dispatch_p2p", _lib.ptr(keep[r][0]), _lib.ptr(keep[r][1]), T, k, H,
+                  n_ranks, r, epr, cap, arr("recv_x"), arr("recv_eid"), arr("flag_d"),
+                  _lib.ptr(srcs[r]), _lib.ptr(ovf), _lib.ptr(bufs[r]["epoch"]),
+                  _lib.ptr(bufs[r]["ctr"]), st)
+    for r in range(n_ranks):
+        _lib.call("d3_ep_wait", _lib.ptr(bufs[r]["flag_d"]), n_ranks, _lib.ptr(bufs[r]["epoch"]),
+                  _lib.ptr(err), 31, 1_000_000_000, st)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and int(ovf.item()) == 0
+    packed = [ref.pack(xs[r], ids[r], n_ranks, epr, cap) for r in range(n_ranks)]
+    for d in range(n_ranks):
+        assert bufs[d]["flag_d"].tolist() == [1] * n_ranks
+        for r in range(n_ranks):
+            sx, se, _ = packed[r]
+            blk = slice(r * cap, (r + 1) * cap)
+            want_e = se[d * cap:(d + 1) * cap]
+            assert torch.equal(bufs[d]["recv_eid"][blk].cpu(), want_e)
+            used = want_e >= 0
+            assert torch.equal(bufs[d]["recv_x"][blk].cpu()[used], sx[d * cap:(d + 1) * cap][used])
+    for r in range(n_ranks):
+        assert torch.equal(srcs[r].cpu(), packed[r][2])
+    # return path: each serving rank sends y = recv_x + 1 back
+    ys = [(b["recv_x"].float() + 1).to(torch.bfloat16) for b in bufs]
+    for d in range(n_ranks):
+        _lib.call("d3_ep_return_p2p", _lib.ptr(ys[d]), _lib.ptr(bufs[d]["recv_eid"]), n_ranks, d,
+                  cap, H, arr("ret"), arr("flag_r"), _lib.ptr(bufs[d]["epoch"]),
+                  _lib.ptr(bufs[d]["ctr"][1:]), st)
+    for r in range(n_ranks):
+        _lib.call("d3_ep_wait", _lib.ptr(bufs[r]["flag_r"]), n_ranks, _lib.ptr(bufs[r]["epoch"]),
+                  _lib.ptr(err), 32, 1_000_000_000, st)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for r in range(n_ranks):
+        for d in range(n_ranks):
+            se = packed[r][1][d * cap:(d + 1) * cap]
+            used = (se >= 0).nonzero().flatten()
+            got = bufs[r]["ret"][d * cap:(d + 1) * cap].cpu()[used]
+            want = ys[d][r * cap:(r + 1) * cap].cpu()[used]
+            assert torch.equal(got, want)
+
+
+def test_p2p_wait_gives_up_and_reports():
+    """A flag nothing sets: the bounded wait ends after its budget with the
+    error code in the error word, and the stream stays usable."""
+    flags = torch.zeros(4, dtype=torch.int64, device=DEV)
+    epoch = torch.ones(1, dtype=torch.int64, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _lib.call("d3_ep_wait", _lib.ptr(flags), 4, _lib.ptr(epoch), _lib.ptr(err), 31, 20_000_000,
+              _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 31
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -65,7 +151,7 @@ def _port():
     return p
 
 
-def _ep_worker(rank, world, port, q):
+def _ep_worker(rank, world, port, q, exchange="p2p"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -78,10 +164,24 @@ def _ep_worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         tr = uniform_trace(steps=4, tokens=16, layers=2, experts=256, k=8)
         m = ExpertParallelMoE(layers=2, global_batch=16, rank=rank, world=world,
-                              device=dev, trace=tr)
+                              device=dev, trace=tr, exchange=exchange)
         h0 = m.h.clone()
         m.step()
         torch.cuda.synchronize()
+        moe.check_errors(dev)
+        # the same step through a captured graph replays to the same result
+        h_eager = m.h.clone()
+        m.h.copy_(h0)
+        m.step_idx.zero_()
+        g = m.capture()
+        m.h.copy_(h0)
+        m.step_idx.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        moe.check_errors(dev)
+        assert torch.equal(m.h, h_eager), "graph replay differs from the eager step"
+        del g
+        m.close()
         hs = [torch.zeros_like(m.h) for _ in range(world)]
         h0s = [torch.zeros_like(h0) for _ in range(world)]
         dist.all_gather(hs, m.h)
@@ -115,12 +215,13 @@ def _ep_worker(rank, world, port, q):
 
 @pytest.mark.skipif(not cuda_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
-def test_ep_two_gpus_matches_single_gpu():
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_two_gpus_matches_single_gpu(exchange):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
