@@ -17,7 +17,8 @@
 //   selects.  No global scratch.
 // * T > 2: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one expert
 //   per warp over a tile of 8 tokens staged in shared memory (each gate row is
-//   read once per token tile).  The last CTA of a token tile to finish (a
+//   read once per token tile); up to 64 tokens each expert is split over 4
+//   warps (2 experts per CTA, 4x the CTAs), the partial sums added in order.  The last CTA of a token tile to finish (a
 //   global arrival counter, reset by that CTA for the next launch or graph
 //   replay) selects the top-k of its tokens from the workspace logits.
 // Selection: one warp per token, logits 32-strided over the lanes, k rounds of
@@ -153,6 +154,8 @@ constexpr int kRouterClusterThreads = 512;
 // grows with the token count; it is used for 1-2 tokens, where it beats the
 // general kernel (measured on B200).
 constexpr int kRouterClusterMaxT = 2;
+// Up to this many tokens the general kernel splits each expert over 4 warps.
+constexpr int kRouterKSplitMaxT = 64;
 constexpr int kRouterXChunk = 10;            // doubles per padded 8-element chunk
 
 __device__ __forceinline__ unsigned cluster_ctarank() {
@@ -270,11 +273,16 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
   topk_select<KPER>(v, per, warp, p);
 }
 
-template <int KPER>
+// KS warps share one expert's dot products (a quarter of H each for KS = 4):
+// the same fp64 work spread over KS times more SMs for mid-sized batches,
+// the partial sums combined in a fixed order in shared memory.
+template <int KPER, int KS>
 __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
+  constexpr int EPC = kRouterExpertsPerCta / KS;   // experts per CTA
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [8][H]
   __shared__ bool s_last;
+  __shared__ double s_part[KS][EPC][kRouterTokensPerCta];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * kRouterTokensPerCta;
   const int nt = min(kRouterTokensPerCta, p.T - t0);
@@ -286,26 +294,28 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
         reinterpret_cast<const uint4*>(p.x + (size_t)(t0 + r) * p.H)[c];
   }
   __syncthreads();
-  const int e = blockIdx.x * kRouterExpertsPerCta + warp;
-  if (e < p.E) {
-    double acc[kRouterTokensPerCta];
+  const int el = warp / KS, kq = warp - (warp / KS) * KS;
+  const int e = blockIdx.x * EPC + el;
+  const int cbeg = kq * (vec_per_row / KS), cend = cbeg + vec_per_row / KS;
+  double acc[kRouterTokensPerCta];
 #pragma unroll
-    for (int t = 0; t < kRouterTokensPerCta; ++t) acc[t] = 0.0;
+  for (int t = 0; t < kRouterTokensPerCta; ++t) acc[t] = 0.0;
+  if (e < p.E) {
     const uint4* wrow = reinterpret_cast<const uint4*>(p.w + (size_t)e * p.H);
-    // issue all of a lane's gate-row loads (8 x 16 B for H = 2048) before any
-    // arithmetic, so the row streams in one memory latency
+    // issue all of a lane's gate-row loads before any arithmetic, so the
+    // row streams in one memory latency
     constexpr int kU = 8;
-    for (int c0 = lane; c0 < vec_per_row; c0 += 32 * kU) {
+    for (int c0 = cbeg + lane; c0 < cend; c0 += 32 * kU) {
       uint4 wv[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int c = c0 + 32 * u;
-        wv[u] = c < vec_per_row ? __ldg(wrow + c) : make_uint4(0, 0, 0, 0);
+        wv[u] = c < cend ? __ldg(wrow + c) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int c = c0 + 32 * u;
-        if (c >= vec_per_row) break;
+        if (c >= cend) break;
         const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
         double wd[8];
 #pragma unroll
@@ -322,16 +332,27 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
         }
       }
     }
+  }
 #pragma unroll
-    for (int t = 0; t < kRouterTokensPerCta; ++t) {
-      if (t < nt) {
-        double v = acc[t];
+  for (int t = 0; t < kRouterTokensPerCta; ++t) {
+    if (t < nt) {
+      double v = acc[t];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) p.logits[(size_t)(t0 + t) * p.E + e] = exact_bf16_of(v);
-      }
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) s_part[kq][el][t] = v;
     }
-    if (lane == 0) __threadfence();  // the logit stores before this CTA's arrival
+  }
+  __syncthreads();
+  if (threadIdx.x < EPC * nt) {
+    const int ee = threadIdx.x / nt, t = threadIdx.x - ee * nt;
+    const int eg = blockIdx.x * EPC + ee;
+    if (eg < p.E) {
+      double v = s_part[0][ee][t];
+#pragma unroll
+      for (int k = 1; k < KS; ++k) v += s_part[k][ee][t];
+      p.logits[(size_t)(t0 + t) * p.E + eg] = exact_bf16_of(v);
+    }
+    __threadfence();  // the logit stores before this CTA's arrival
   }
   // last CTA of this token tile does the selection
   __syncthreads();
@@ -388,10 +409,15 @@ static int launch_router(const RouterParams& p, cudaStream_t st, const char* wha
     D3_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, p), what);
     return D3_OK;
   }
-  const dim3 grid((unsigned)((p.E + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta),
+  // mid-sized batches split each expert's dot products over 4 warps (4x the
+  // CTAs); large batches already fill the GPU with token tiles
+  const bool ksplit = p.T <= kRouterKSplitMaxT && p.H % 32 == 0;
+  const int epc = ksplit ? kRouterExpertsPerCta / 4 : kRouterExpertsPerCta;
+  const dim3 grid((unsigned)((p.E + epc - 1) / epc),
                   (unsigned)((p.T + kRouterTokensPerCta - 1) / kRouterTokensPerCta));
   const size_t smem = (size_t)kRouterTokensPerCta * p.H * sizeof(__nv_bfloat16);
-  void (*k)(RouterParams) = small_e ? router_kernel<8> : router_kernel<32>;
+  void (*k)(RouterParams) = ksplit ? (small_e ? router_kernel<8, 4> : router_kernel<32, 4>)
+                                   : (small_e ? router_kernel<8, 1> : router_kernel<32, 1>);
   if (smem > 48 * 1024)
     D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "router smem attribute");
