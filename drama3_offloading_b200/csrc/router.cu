@@ -17,7 +17,7 @@
 //   selects.  No global scratch.
 // * T > 2: grid (E / 8 experts, ceil(T / 8) token tiles), 8 warps, one expert
 //   per warp over a tile of 8 tokens staged in shared memory (each gate row is
-//   read once per token tile); up to 64 tokens each expert is split over 4
+//   read once per token tile); up to 16 tokens each expert is split over 4
 //   warps (2 experts per CTA, 4x the CTAs), the partial sums added in order.  The last CTA of a token tile to finish (a
 //   global arrival counter, reset by that CTA for the next launch or graph
 //   replay) selects the top-k of its tokens from the workspace logits.
@@ -154,8 +154,11 @@ constexpr int kRouterClusterThreads = 512;
 // grows with the token count; it is used for 1-2 tokens, where it beats the
 // general kernel (measured on B200).
 constexpr int kRouterClusterMaxT = 2;
-// Up to this many tokens the general kernel splits each expert over 4 warps.
-constexpr int kRouterKSplitMaxT = 64;
+// Up to this many tokens the general kernel splits each expert over 4 warps
+// (measured on B200: 9.4 / 10.8 us at 8 / 16 tokens against 15.0 / 15.0 us
+// unsplit; at 64 tokens the 4x CTA count costs more than it gains: 28.7 vs
+// 20.0 us).
+constexpr int kRouterKSplitMaxT = 16;
 constexpr int kRouterXChunk = 10;            // doubles per padded 8-element chunk
 
 __device__ __forceinline__ unsigned cluster_ctarank() {
