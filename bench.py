@@ -624,24 +624,45 @@ def run_ep(args, rank, world, local):
         torch.cuda.synchronize(dev)
     benchutil.barrier(world, dev)
     ms = benchutil.max_over_ranks(a.elapsed_time(b), world, dev)
-    # expert-GEMM time per rank from an eager sample, bytes from the trace
-    start = int(m.step_idx.item())
-    evs = []
-    sample = 4
-    for _ in range(sample):
-        m.step(gemm_events=evs)
-    torch.cuda.synchronize(dev)
-    gemm_ms = sum(x.elapsed_time(y) for x, y in evs)
-    lo, hi = rank * m.epr, (rank + 1) * m.epr
-    distinct = 0
-    for s in range(sample):
-        row = trace[(start + s) % trace.shape[0]]
-        for l in range(args.layers):
-            u = np.unique(row[l].reshape(-1))
-            distinct += int(((u >= lo) & (u < hi)).sum())
+    # the expert call per rank, timed as it runs in the step -- replayed from a
+    # CUDA graph with CUDA events -- on the rows this rank received last, for
+    # each layer's weights; bytes = the distinct local experts in those rows
     eb = synth_expert_bytes(2048, 512)
-    gemm_bytes = distinct * eb
-    gemm_gbs = gemm_bytes / (gemm_ms * 1e-3) / 1e9
+    per_layer_us, per_layer_bytes = [], []
+    reps = 10
+    for l in range(args.layers):
+        wl = m.w[l]
+        if m.exchange == "none":
+            cur = m.trace_dev.index_select(0, m.step_idx)[0][l]
+            xin, ids_in, w_in = m.h, cur, m.wts
+        else:
+            bufs = m.p2p if m.p2p is not None else m
+            xin, ids_in, w_in = bufs.recv_x, bufs.recv_eid.view(-1, 1), m.ones
+        fn = lambda: moe.fp8_moe_forward(xin, ids_in, w_in, wl.w13_weight, wl.w13_scale_inv,
+                                         wl.w2_weight, wl.w2_scale_inv, out=m.y if
+                                         m.exchange != "none" else None)
+        s_ = torch.cuda.Stream(device=dev)
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
+            fn()
+        torch.cuda.current_stream().wait_stream(s_)
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            for _ in range(reps):
+                fn()
+        gg.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gg.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        per_layer_us.append(e0.elapsed_time(e1) * 1e3 / reps)
+        used = ids_in.reshape(-1).cpu().numpy()
+        used = used[(used >= 0) & (used < m.epr)] if m.exchange != "none" else used
+        per_layer_bytes.append(len(np.unique(used)) * eb)
+        del gg
+    gemm_us = float(np.mean(per_layer_us))
+    gemm_gbs = float(np.sum(per_layer_bytes)) / (float(np.sum(per_layer_us)) * 1e-6) / 1e9
     hbm = measured_peaks()["hbm_gbs"]
     gbs_all = [0.0] * world
     if world > 1:
@@ -672,10 +693,13 @@ def run_ep(args, rank, world, local):
                    "parallelism": f"ep{world}", "exchange": exch,
                    "l2": f"inputs > L2 ({args.layers * m.epr * eb / 2**30:.1f} GiB resident "
                          f"experts per GPU)"},
+        "expert_call_us": gemm_us,
         "roofline": {"bound": "hbm", "kernel": "expert GEMMs (d3_moe_fp8_forward, per rank)",
                      "achieved": gemm_gbs, "peak": hbm, "unit": "GB/s", "frac": gemm_gbs / hbm,
                      "traffic": None, "per_rank_gbs": gbs_all,
                      "bytes": "distinct local experts x 3,146,496 B per layer",
+                     "timing": "the rank's expert call replayed from a CUDA graph (10 calls) "
+                               "per layer on its last received rows, CUDA events",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "overflow_pairs": overflow, "clocks": clk.summary(),
         "gpu_launches": args.steps * args.layers * per_layer,
