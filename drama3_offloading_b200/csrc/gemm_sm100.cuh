@@ -56,7 +56,13 @@ struct GemmCfg {
   static constexpr int KB_BYTES = A_BYTES + 2 * B_BYTES;   // one K-block
   static constexpr int STAGE_BYTES = KPS * KB_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  // accumulator buffers in TMEM (one per K-block in flight) and the number of
+  // K-blocks the epilogue promotes per round: the MMA runs up to NB K-blocks
+  // ahead of the epilogue, which loads G accumulators back to back and waits
+  // once, so the per-K-block TMEM round trip no longer paces the MMA.
+  static constexpr int NB = BN >= 64 ? 4 : 8;
+  static constexpr int G = BN >= 64 ? 2 : 4;
+  static constexpr int TMEM_COLS = NB * BN;
   static constexpr int EPI = BN >= 64 ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI;
   static constexpr int CPT = BN * 4 / EPI;
@@ -84,18 +90,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
   float* s_scale = reinterpret_cast<float*>(smem + (size_t)S * Cfg::STAGE_BYTES);  // [kb][BN]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * Cfg::STAGE_BYTES +
                                                Cfg::SCALE_BYTES);
-  uint64_t* full = bars;             // [S]
-  uint64_t* empty = bars + S;        // [S]
-  uint64_t* accf = bars + 2 * S;     // [2]
-  uint64_t* acce = bars + 2 * S + 2; // [2]
-  uint64_t* done = bars + 2 * S + 4; // [1]
+  constexpr int NB = Cfg::NB;
+  uint64_t* full = bars;                   // [S]
+  uint64_t* empty = bars + S;              // [S]
+  uint64_t* accf = bars + 2 * S;           // [NB]
+  uint64_t* acce = bars + 2 * S + NB;      // [NB]
+  uint64_t* done = bars + 2 * S + 2 * NB;  // [1]
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(accf + i, 1); mbar_init(acce + i, 32 * Cfg::EPI); }
+    for (int i = 0; i < NB; ++i) { mbar_init(accf + i, 1); mbar_init(acce + i, 32 * Cfg::EPI); }
     mbar_init(done, 1);
     s_abort = 0;
     fence_barrier_init();
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
           const int nk = min(KPS, kb1 - kb);
           const uint32_t st = smem_u32(stage_base + (size_t)stage * Cfg::STAGE_BYTES);
           for (int q = 0; q < nk; ++q, ++it) {
-            const uint32_t ab = it & 1, aph = (it >> 1) & 1;
+            const uint32_t ab = it % NB, aph = (it / NB) & 1;
             if (!mbar_wait(acce + ab, aph ^ 1, kGemmWaitBudgetNs)) {
               gemm_error(p.err, 2); s_abort = 1; ok = false; break;
             }
@@ -234,31 +241,50 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
 #pragma unroll
       for (int n = 0; n < CPT; ++n) r[n] = 0.f;
       bool ok = true;
-      for (int j = 0; j < nkb; ++j, ++it) {
-        const uint32_t ab = it & 1, aph = (it >> 1) & 1;
-        if (!ok) continue;
-        if (!mbar_wait(accf + ab, aph, kGemmWaitBudgetNs)) {
-          gemm_error(p.err, 4); s_abort = 1; ok = false; continue;
-        }
-        tc_fence_after();
-        const float4* sc = reinterpret_cast<const float4*>(s_scale + j * BN + col0);
-#pragma unroll
-        for (int c16 = 0; c16 < CPT / 16; ++c16) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + ab * BN + c16 * 16, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const float4 s4 = sc[c16 * 4 + c4];
-            const int n = c16 * 16 + c4 * 4;
-            r[n + 0] = fmaf(s4.x, __uint_as_float(v[c4 * 4 + 0]), r[n + 0]);
-            r[n + 1] = fmaf(s4.y, __uint_as_float(v[c4 * 4 + 1]), r[n + 1]);
-            r[n + 2] = fmaf(s4.z, __uint_as_float(v[c4 * 4 + 2]), r[n + 2]);
-            r[n + 3] = fmaf(s4.w, __uint_as_float(v[c4 * 4 + 3]), r[n + 3]);
+      constexpr int G = Cfg::G;
+      for (int j0 = 0; j0 < nkb; j0 += G) {
+        const int g = min(G, nkb - j0);
+        if (ok) {
+          for (int jj = 0; jj < g; ++jj) {
+            const uint32_t b = (it + jj) % NB, ph = ((it + jj) / NB) & 1;
+            if (!mbar_wait(accf + b, ph, kGemmWaitBudgetNs)) {
+              gemm_error(p.err, 4); s_abort = 1; ok = false; break;
+            }
           }
         }
-        tc_fence_before();
-        mbar_arrive(acce + ab);
+        if (ok) {
+          tc_fence_after();
+          uint32_t v[G][CPT];
+#pragma unroll
+          for (int jj = 0; jj < G; ++jj) {
+            if (jj < g) {
+              const uint32_t b = (it + jj) % NB;
+#pragma unroll
+              for (int c16 = 0; c16 < CPT / 16; ++c16) {
+                uint32_t (&vv)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[jj][c16 * 16]);
+                tmem_ld16(lane_base + b * BN + c16 * 16, vv);
+              }
+            }
+          }
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < G; ++jj) {
+            if (jj < g) {
+              const float4* sc = reinterpret_cast<const float4*>(s_scale + (j0 + jj) * BN + col0);
+#pragma unroll
+              for (int c4 = 0; c4 < CPT / 4; ++c4) {
+                const float4 s4 = sc[c4];
+                r[4 * c4 + 0] = fmaf(s4.x, __uint_as_float(v[jj][4 * c4 + 0]), r[4 * c4 + 0]);
+                r[4 * c4 + 1] = fmaf(s4.y, __uint_as_float(v[jj][4 * c4 + 1]), r[4 * c4 + 1]);
+                r[4 * c4 + 2] = fmaf(s4.z, __uint_as_float(v[jj][4 * c4 + 2]), r[4 * c4 + 2]);
+                r[4 * c4 + 3] = fmaf(s4.w, __uint_as_float(v[jj][4 * c4 + 3]), r[4 * c4 + 3]);
+              }
+            }
+          }
+          tc_fence_before();
+          for (int jj = 0; jj < g; ++jj) mbar_arrive(acce + (it + jj) % NB);
+        }
+        it += g;
       }
       if (!ok) continue;  // leaves at the next tile's shared abort decision
       const int split = tl.y >> 16;  // K-split index of this tile
