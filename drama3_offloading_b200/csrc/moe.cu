@@ -9,28 +9,30 @@
 // where W = e4m3 bytes x fp32 scale per 128x128 block.
 //
 // Pipeline (all launches static-shaped, sync-free, graph-capturable):
-//   1. route   one CTA: counting sort of the pairs by expert (stable), tile
-//              lists for both GEMMs (expert, 128-row M tile, N tile of pairs,
-//              K-split), written to the workspace.
-//   2. quant   activations of every sorted pair -> two e4m3 planes hi/lo per
-//              128-wide K block with one fp32 scale: x ~= s*(hi + lo), where
-//              hi = e4m3(x/s) and lo = e4m3(x/s - hi).  Two fp8 planes carry
-//              ~8 significant bits, i.e. bf16-class activations on the fp8
-//              tensor path.
-//   3. gemm1   tcgen05 kind::f8f6f4: D[128 weight rows, BN pairs] per K block
+//   1. route   G CTAs, each computing the same stable counting sort of the
+//              pairs by expert; together they write the tile lists for both
+//              GEMMs (expert, 128-row M tile, N tile of pairs, K-split) and
+//              quantise the activations of every sorted pair into two e4m3
+//              planes hi/lo per 128-wide K block with one fp32 scale:
+//              x ~= s*(hi + lo), hi = e4m3(x/s), lo = e4m3(x/s - hi).  Two
+//              fp8 planes carry ~8 significant bits, i.e. bf16-class
+//              activations on the fp8 tensor path.  (Above 4096 pairs the
+//              quantisation is its own launch.)
+//   2. gemm1   tcgen05 kind::f8f6f4: D[128 weight rows, BN pairs] per K block
 //              = W.hi + W.lo accumulated in TMEM, TMA-staged operands (128B
 //              swizzle); the epilogue warps promote each K block with
 //              s_w[kb] * s_x[n,kb] into fp32 registers (per-block scales, the
 //              DeepSeek-style promotion), then store the K-split partials.
-//   4. act     sum the K-split partials, SwiGLU, quantise h into hi/lo planes.
-//   5. gemm2   same kernel over W2 (K = I).
-//   6. combine out[t] = bf16(sum_k w[t,k] * y[pair(t,k)]) in a fixed order.
+//   3. act     sum the K-split partials, SwiGLU, quantise h into hi/lo planes.
+//   4. gemm2   same kernel over W2 (K = I).
+//   5. combine out[t] = bf16(sum_k w[t,k] * y[pair(t,k)]) in a fixed order.
 // Swap-AB: weight rows are the MMA M dimension (128), routed tokens the N
 // dimension (16 for decode-sized batches, 64 otherwise), so one decode token
 // still runs full-height MMAs.  The GEMMs stream each weight byte from HBM
 // once per N tile; K-splits spread a small batch's few experts over all SMs.
 #include "d3_common.cuh"
 #include "gemm_sm100.cuh"
+#include "moe_epilogue.cuh"
 #include "moe_gemv.cuh"
 
 #include <cuda.h>
@@ -85,7 +87,8 @@ static int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_
 
 constexpr int kMaxExperts = 8192;
 constexpr int kMaxPairs = 65536;
-constexpr int kFusedQuantMaxPairs = 256;   // route quantises in-launch up to this many pairs
+constexpr int kFusedQuantMaxPairs = 4096;  // route quantises in-launch up to this many pairs
+constexpr int kRouteSmemBudget = 160 * 1024;  // route launch: shared memory for the sort
 
 struct Plan {
   int P;        // routed pairs = T * topk
@@ -154,7 +157,8 @@ struct RouteParams {
   int mt1, nkb1, split1_min, split1_max;
   int mt2, nkb2, split2_min, split2_max;
   int sms;
-  // activation quantisation folded into this launch for small batches
+  int nw;  // warps (chunks) of the stable sort
+  // activation quantisation folded into this launch
   int fuse_quant;
   const __nv_bfloat16* x; int topk, H, Ppad;
   uint8_t* xq; float* xs;
@@ -188,41 +192,80 @@ __device__ __forceinline__ int pick_split(int tiles, int nkb, int lo, int hi, in
   return (nkb + per - 1) / per;
 }
 
-// One CTA of 1024 threads; dynamic smem: cursor[n] + tile prefix[n].
+// Grid of G CTAs x 1024 threads.  Every CTA computes the same stable
+// counting sort of the pairs by expert in its own shared memory (no
+// cross-CTA communication; identical inputs give identical results), then
+// the CTAs share the writing: the tile lists (one entry per thread,
+// grid-strided), the fused activation quantisation (one warp per sorted row
+// x K block, grid-strided) and, from CTA 0 only, the per-pair tables.
+//
+// The stable sort runs NW warps over NW consecutive chunks of the pairs:
+// pass 1 counts each expert per chunk (hist[w][e]), a column scan over the
+// chunks turns the counts into chunk-local bases, and pass 2 places every
+// pair at off[e] + base[w][e] + (rank among the equal ids of its 32-pair
+// batch) -- exactly the order of a sequential walk.
+// Dynamic shared memory (ints): cnt[n], off[n], tile prefix[n], hist[NW][n],
+// then sorted[P] when the quantisation is fused.
+__device__ __forceinline__ int route_chunk(int P, int nw) {
+  const int batches = (P + 31) / 32;
+  return (batches + nw - 1) / nw * 32;
+}
+
 __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   extern __shared__ int sm[];
-  int* cursor = sm;            // [n]
-  int* tcount = sm + p.n;      // [n] N tiles per expert, then its prefix
-  __shared__ int warp_tot[32];
-  __shared__ int s_sorted[kFusedQuantMaxPairs];  // row -> pair, for the fused quantisation
+  const int n = p.n, NW = p.nw;
+  int* s_cnt = sm;                // [n]
+  int* s_off = sm + n;            // [n]
+  int* s_tp = sm + 2 * n;         // [n] exclusive prefix of N tiles per expert
+  int* hist = sm + 3 * n;         // [NW][n]
+  int* s_sorted = hist + (size_t)NW * n;  // [P] (fused quantisation only)
+  __shared__ int warp_tot[32], wt2[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool lead = blockIdx.x == 0;
   pdl_trigger();
   pdl_wait();
-  for (int e = tid; e < p.n; e += blockDim.x) cursor[e] = 0;
+  for (int i = tid; i < NW * n; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  for (int i = tid; i < p.P; i += blockDim.x) {
-    const int e = load_pair_id(p.ids, p.ids_bytes, i, p.n);
-    if (e >= 0) atomicAdd(&cursor[e], 1);
-    p.inv[i] = -1;
+  const int C = route_chunk(p.P, NW);
+  // ---- pass 1: per-chunk counts (leaders of a batch hold distinct ids)
+  if (warp < NW) {
+    int* h = hist + (size_t)warp * n;
+    const int end = min(p.P, (warp + 1) * C);
+    for (int b0 = warp * C; b0 < end; b0 += 32) {
+      const int i = b0 + lane;
+      const int e = i < end ? load_pair_id(p.ids, p.ids_bytes, i, n) : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && lane == __ffs(m) - 1) h[e] += __popc(m);
+      __syncwarp();
+    }
   }
   __syncthreads();
-  // exclusive scans of counts (-> offsets) and of N tiles per expert
-  const int per = (p.n + blockDim.x - 1) / blockDim.x;
-  const int lo = tid * per, hi = min(p.n, lo + per);
-  int s_cnt = 0, s_til = 0;
+  // ---- column scan: chunk-local bases, totals per expert
+  for (int e = tid; e < n; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < NW; ++w) {
+      const int c = hist[(size_t)w * n + e];
+      hist[(size_t)w * n + e] = run;
+      run += c;
+    }
+    s_cnt[e] = run;
+  }
+  __syncthreads();
+  // ---- exclusive scans of counts (-> offsets) and of N tiles per expert
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = tid * per, hi = min(n, lo + per);
+  int s_c = 0, s_t = 0;
   for (int e = lo; e < hi; ++e) {
-    const int c = cursor[e];
-    s_cnt += c;
-    s_til += (c + p.BN - 1) / p.BN;
+    const int c = s_cnt[e];
+    s_c += c;
+    s_t += (c + p.BN - 1) / p.BN;
   }
-  // block scan of (s_cnt, s_til) packed as two ints via two passes
-  int v = s_cnt, w = s_til;
+  int v = s_c, w = s_t;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int a = __shfl_up_sync(0xffffffffu, v, o), b = __shfl_up_sync(0xffffffffu, w, o);
     if (lane >= o) { v += a; w += b; }
   }
-  __shared__ int wt2[32];
   if (lane == 31) { warp_tot[warp] = v; wt2[warp] = w; }
   __syncthreads();
   if (warp == 0) {
@@ -235,129 +278,120 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
     warp_tot[lane] = a; wt2[lane] = b;
   }
   __syncthreads();
-  int base_c = (v - s_cnt) + (warp > 0 ? warp_tot[warp - 1] : 0);
-  int base_t = (w - s_til) + (warp > 0 ? wt2[warp - 1] : 0);
-  const int total_ntiles = wt2[31];
-  for (int e = lo; e < hi; ++e) {
-    const int c = cursor[e];
-    p.cnt[e] = c;
-    p.off[e] = base_c;
-    const int t = (c + p.BN - 1) / p.BN;
-    tcount[e] = base_t;
-    cursor[e] = base_c;
-    base_c += c;
-    base_t += t;
+  {
+    int base_c = (v - s_c) + (warp > 0 ? warp_tot[warp - 1] : 0);
+    int base_t = (w - s_t) + (warp > 0 ? wt2[warp - 1] : 0);
+    for (int e = lo; e < hi; ++e) {
+      const int c = s_cnt[e];
+      s_off[e] = base_c;
+      s_tp[e] = base_t;
+      if (lead) { p.cnt[e] = c; p.off[e] = base_c; }
+      base_c += c;
+      base_t += (c + p.BN - 1) / p.BN;
+    }
   }
+  const int nvalid = warp_tot[31], total_ntiles = wt2[31];
   __syncthreads();
-  // stable placement: warp 0 walks the pairs in order, 32 at a time
-  if (warp == 0) {
-    for (int b0 = 0; b0 < p.P; b0 += 32) {
+  // ---- pass 2: stable placement
+  if (warp < NW) {
+    int* h = hist + (size_t)warp * n;
+    const int end = min(p.P, (warp + 1) * C);
+    for (int b0 = warp * C; b0 < end; b0 += 32) {
       const int i = b0 + lane;
-      const int e = i < p.P ? load_pair_id(p.ids, p.ids_bytes, i, p.n) : -1;
+      const int e = i < end ? load_pair_id(p.ids, p.ids_bytes, i, n) : -1;
       const unsigned m = __match_any_sync(0xffffffffu, e);
       const int leader = __ffs(m) - 1;
-      const int rank = __popc(m & ((1u << lane) - 1));
       int base = 0;
-      if (lane == leader && e >= 0) {
-        base = cursor[e];
-        cursor[e] = base + __popc(m);
+      if (e >= 0 && lane == leader) {
+        base = h[e];
+        h[e] = base + __popc(m);
       }
       base = __shfl_sync(0xffffffffu, base, leader);
-      if (e >= 0) {
-        const int pos = base + rank;
-        p.sorted[pos] = i;
-        if (p.fuse_quant) s_sorted[pos] = i;  // fuse_quant implies P <= kFusedQuantMaxPairs
-        p.inv[i] = pos;
+      if (i < end) {
+        int pos = -1;
+        if (e >= 0) {
+          pos = s_off[e] + base + __popc(m & ((1u << lane) - 1));
+          if (p.fuse_quant) s_sorted[pos] = i;
+          if (lead) p.sorted[pos] = i;
+        }
+        if (lead) p.inv[i] = pos;
       }
       __syncwarp();
     }
   }
   // sorted positions past the valid pairs (skipped ids) hold -1
-  for (int i = warp_tot[31] + tid; i < p.P; i += blockDim.x) p.sorted[i] = -1;
+  if (lead)
+    for (int i = nvalid + tid; i < p.P; i += blockDim.x) p.sorted[i] = -1;
   __syncthreads();
+  const int gthreads = gridDim.x * blockDim.x;
+  const int gtid = blockIdx.x * blockDim.x + tid;
   if (p.fuse_quant) {
     // only the valid rows: the GEMM never uses a column past an expert's
     // pair count, so padding rows need no planes; four blocks per warp with
     // their loads issued together
     const int nkb = p.H / 128;
-    const int nblk = warp_tot[31] * nkb;
-    for (int w0 = warp * 4; w0 < nblk; w0 += 32 * 4) {
-      float v[4][4];
+    const int nblk = nvalid * nkb;
+    const int gwarps = gthreads >> 5;
+    for (int w0 = (gtid >> 5) * 4; w0 < nblk; w0 += gwarps * 4) {
+      float xv[4][4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int w = w0 + u;
-        if (w < nblk) {
-          const int row = w / nkb, kb = w - row * nkb;
-          load_x_block(p.x, s_sorted[row], p.topk, p.H, kb, v[u]);
+        const int wu = w0 + u;
+        if (wu < nblk) {
+          const int row = wu / nkb, kb = wu - row * nkb;
+          load_x_block(p.x, s_sorted[row], p.topk, p.H, kb, xv[u]);
         }
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int w = w0 + u;
-        if (w < nblk) {
-          const int row = w / nkb, kb = w - row * nkb;
-          store_x_block(v[u], p.H, row, kb, p.xq, p.xs);
+        const int wu = w0 + u;
+        if (wu < nblk) {
+          const int row = wu / nkb, kb = wu - row * nkb;
+          store_x_block(xv[u], p.H, row, kb, p.xq, p.xs);
         }
       }
     }
   }
-  // tile lists: for expert e, N tile j, split s, M tile m; the K split from
-  // the real number of N tiles
+  // ---- tile lists: entry (N tile nt, split s, M tile m) at nt*per + s*mt + m;
+  // the K split from the real number of N tiles
   int kbps1, kbps2;
   const int split1 = pick_split(total_ntiles * p.mt1, p.nkb1, p.split1_min, p.split1_max, p.sms,
                                 &kbps1);
   const int split2 = pick_split(total_ntiles * p.mt2, p.nkb2, p.split2_min, p.split2_max, p.sms,
                                 &kbps2);
   const int per_nt1 = p.mt1 * split1, per_nt2 = p.mt2 * split2;
-  for (int e = lo; e < hi; ++e) {
-    const int c = p.cnt[e];
-    if (c == 0) continue;
-    const int ntl = (c + p.BN - 1) / p.BN;
-    const int t0 = tcount[e];
-    for (int j = 0; j < ntl; ++j) {
-      const int row0 = p.off[e] + j * p.BN;
-      const int nc = min(p.BN, c - j * p.BN);
-      int4* d1 = p.tiles1 + (size_t)(t0 + j) * per_nt1;
-      for (int s = 0; s < split1; ++s)
-        for (int m = 0; m < p.mt1; ++m)
-          d1[s * p.mt1 + m] = pack_tile(e, m, s, row0, nc, s * kbps1,
-                                        min(p.nkb1, (s + 1) * kbps1));
-      int4* d2 = p.tiles2 + (size_t)(t0 + j) * per_nt2;
-      for (int s = 0; s < split2; ++s)
-        for (int m = 0; m < p.mt2; ++m)
-          d2[s * p.mt2 + m] = pack_tile(e, m, s, row0, nc, s * kbps2,
-                                        min(p.nkb2, (s + 1) * kbps2));
+  const int tot1 = total_ntiles * per_nt1, tot2 = total_ntiles * per_nt2;
+  for (int t = gtid; t < tot1 + tot2; t += gthreads) {
+    const bool first = t < tot1;
+    const int tt = first ? t : t - tot1;
+    const int pn = first ? per_nt1 : per_nt2, mt = first ? p.mt1 : p.mt2;
+    const int nt = tt / pn, r = tt - nt * pn;
+    const int sp = r / mt, m = r - sp * mt;
+    // expert: the last e with s_tp[e] <= nt (experts without tiles share the
+    // next one's prefix, so the last such e has tiles)
+    int a = 0, b = n - 1;
+    while (a < b) {
+      const int mid = (a + b + 1) >> 1;
+      if (s_tp[mid] <= nt) a = mid; else b = mid - 1;
     }
+    const int e = a, j = nt - s_tp[e];
+    const int row0 = s_off[e] + j * p.BN;
+    const int nc = min(p.BN, s_cnt[e] - j * p.BN);
+    if (first)
+      p.tiles1[tt] = pack_tile(e, m, sp, row0, nc, sp * kbps1, min(p.nkb1, (sp + 1) * kbps1));
+    else
+      p.tiles2[tt] = pack_tile(e, m, sp, row0, nc, sp * kbps2, min(p.nkb2, (sp + 1) * kbps2));
   }
-  if (tid == 0) {
-    p.ntiles[0] = total_ntiles * per_nt1;
-    p.ntiles[1] = total_ntiles * per_nt2;
-    p.ntiles[2] = warp_tot[31];  // valid (in-range) pairs
-    p.ntiles[3] = split1;        // K splits the partial sums come in
+  if (lead && tid == 0) {
+    p.ntiles[0] = tot1;
+    p.ntiles[1] = tot2;
+    p.ntiles[2] = nvalid;  // valid (in-range) pairs
+    p.ntiles[3] = split1;  // K splits the partial sums come in
     p.ntiles[4] = split2;
   }
 }
 
 // ---------------------------------------------------------------- 2/4. quantise
-
-// hi/lo e4m3 planes of one 128-element block held 4 per lane: returns scale.
-__device__ __forceinline__ float quant_block(const float (&v)[4], uint32_t& hi4, uint32_t& lo4) {
-  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float inv = amax > 0.f ? 448.f / amax : 0.f;
-  hi4 = 0; lo4 = 0;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float y = v[q] * inv;
-    const __nv_fp8_storage_t h = __nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
-    const float hf = __half2float(__nv_cvt_fp8_to_halfraw(h, __NV_E4M3));
-    const __nv_fp8_storage_t l = __nv_cvt_float_to_fp8(y - hf, __NV_SATFINITE, __NV_E4M3);
-    hi4 |= (uint32_t)h << (8 * q);
-    lo4 |= (uint32_t)l << (8 * q);
-  }
-  return amax > 0.f ? amax / 448.f : 0.f;
-}
 
 // One warp, one 128-wide K block of a pair's token row: 4 values per lane.
 __device__ __forceinline__ void load_x_block(const __nv_bfloat16* __restrict__ x, int pair,
@@ -404,71 +438,29 @@ __global__ void quant_x_kernel(const __nv_bfloat16* x, const int* sorted, const 
 
 // One warp per (sorted row, K block of I) of the valid rows: sum splits,
 // SwiGLU, quantise.
-__global__ void act_kernel(const float* ws1, const int* split_ptr, int P, int Ppad,
-                           const int* nvalid_ptr, int I, uint8_t* __restrict__ hq,
-                           float* __restrict__ hs) {
+__global__ void act_kernel(const float* ws1, const int* split_ptr, int P, const int* nvalid_ptr,
+                           int I, uint8_t* __restrict__ hq, float* __restrict__ hs) {
   pdl_trigger();
   pdl_wait();
-  const int split = *split_ptr;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int nkb = I / 128;
   if (gw >= *nvalid_ptr * nkb) return;
   const int row = gw / nkb, kb = gw - row * nkb;
-  (void)Ppad;
-  float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < split; ++s) {
-    const float* r = ws1 + ((size_t)s * P + row) * 2 * I + kb * 128 + lane * 4;
-    const float4 a = *reinterpret_cast<const float4*>(r);
-    const float4 b = *reinterpret_cast<const float4*>(r + I);
-    g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
-    u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
-  }
-  float h[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) h[q] = g[q] / (1.f + expf(-g[q])) * u[q];
-  uint32_t hi4, lo4;
-  const float s = quant_block(h, hi4, lo4);
-  uint8_t* qrow = hq + (size_t)row * 2 * I;
-  *reinterpret_cast<uint32_t*>(qrow + kb * 128 + lane * 4) = hi4;
-  *reinterpret_cast<uint32_t*>(qrow + I + kb * 128 + lane * 4) = lo4;
-  if (lane == 0) hs[(size_t)row * nkb + kb] = s;
+  act_unit(ws1, *split_ptr, P, row, kb, I, hq, hs, lane);
 }
 
-// out[t, j] = bf16( [out[t,j] +] sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order.
+// out[t, j] = bf16( [out[t,j] +] sum_k w[t,k] * sum_s ws2[s][inv[t,k]][j] ), k in order;
+// one warp per (token, 128 columns).
 __global__ void combine_kernel(const float* ws2, const int* split_ptr, int P, int H,
                                const int* inv, const void* weights, int weights_f32, int T,
                                int topk, int accumulate, __nv_bfloat16* out) {
   pdl_trigger();
   pdl_wait();
-  const int split = *split_ptr;
   const int t = blockIdx.y;
-  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-  if (t >= T || j >= H) return;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (accumulate) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(out + (size_t)t * H + j);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) acc[q] = __bfloat162float(b[q]);
-  }
-  for (int k = 0; k < topk; ++k) {
-    const int pos = inv[t * topk + k];
-    if (pos < 0) continue;
-    const float wk = weights_f32 ? static_cast<const float*>(weights)[t * topk + k]
-                                 : __bfloat162float(
-                                       static_cast<const __nv_bfloat16*>(weights)[t * topk + k]);
-    float y[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < split; ++s) {
-      const float4 a = *reinterpret_cast<const float4*>(ws2 + ((size_t)s * P + pos) * H + j);
-      y[0] += a.x; y[1] += a.y; y[2] += a.z; y[3] += a.w;
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) acc[q] = fmaf(wk, y[q], acc[q]);
-  }
-  __nv_bfloat16 o[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) o[q] = __float2bfloat16_rn(acc[q]);
-  *reinterpret_cast<uint2*>(out + (size_t)t * H + j) = *reinterpret_cast<uint2*>(o);
+  const int j0 = (blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * 4;
+  if (t >= T || j0 >= H) return;
+  combine_unit(ws2, *split_ptr, P, H, inv, weights, weights_f32, t, topk, accumulate, out, j0,
+               threadIdx.x & 31);
 }
 
 // ---------------------------------------------------------------- 3/5. GEMM
@@ -636,21 +628,37 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   rp.sms = num_sms();
   uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
   float* xs = (float*)(ws + pl.o_xs);
-  // small batches quantise inside the route launch (one CTA, 32 warps)
-  rp.fuse_quant =
-      ((long)pl.Ppad * (H / 128) <= 32L * 32 && P <= kFusedQuantMaxPairs) ? 1 : 0;
+  // the route launch quantises the activations itself up to
+  // kFusedQuantMaxPairs pairs (its CTAs share the rows)
+  rp.fuse_quant = P <= kFusedQuantMaxPairs ? 1 : 0;
   rp.x = static_cast<const __nv_bfloat16*>(x);
   rp.topk = topk; rp.H = H; rp.Ppad = pl.Ppad; rp.xq = xq; rp.xs = xs;
   const bool pdl = pdl_enabled();
-  const size_t rsmem = sizeof(int) * 2 * (size_t)n_experts;
+  // shared memory: cnt, off, tile prefix [n] + sorted [P] (fused) + NW chunk
+  // histograms of n ints, as many chunks (<= 32, <= the 32-pair batches) as
+  // the budget holds
+  const size_t rbase = sizeof(int) * (3 * (size_t)n_experts + (rp.fuse_quant ? (size_t)P : 0));
+  long nw = ((long)kRouteSmemBudget - (long)rbase) / (long)(sizeof(int) * (size_t)n_experts);
+  nw = nw < 1 ? 1 : (nw > 32 ? 32 : nw);
+  if (nw > (P + 31) / 32) nw = (P + 31) / 32;
+  rp.nw = (int)nw;
+  const size_t rsmem = rbase + sizeof(int) * (size_t)nw * n_experts;
   if (rsmem > 48 * 1024)
     D3_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)rsmem),
                 "route smem attribute");
+  // CTAs: enough for one sweep of the quantisation (4 blocks per warp) and
+  // of the tile lists (4 entries per thread)
+  long rgrid = (long)(pl.maxt1 + pl.maxt2 + 4095) / 4096;
+  if (rp.fuse_quant) {
+    const long q = ((long)P * (H / 128) + 127) / 128;
+    if (q > rgrid) rgrid = q;
+  }
+  rgrid = rgrid < 1 ? 1 : (rgrid > num_sms() ? num_sms() : rgrid);
   // The first launch of a call is an ordinary stream dependent: whatever the
   // caller queued before it (copies, foreign kernels) must complete first;
   // only the launches inside this call are chained programmatically.
-  D3_CUDA_TRY(launch_k(route_kernel, dim3(1), dim3(1024), rsmem, st, false, rp),
+  D3_CUDA_TRY(launch_k(route_kernel, dim3((unsigned)rgrid), dim3(1024), rsmem, st, false, rp),
               "route_kernel launch");
   int rc = D3_OK;
   if (!rp.fuse_quant) {
@@ -678,7 +686,7 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   {
     const long warps = (long)pl.Ppad * (I / 128);
     D3_CUDA_TRY(launch_k(act_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st,
-                         pdl, (const float*)ws1, (const int*)(rp.ntiles + 3), P, pl.Ppad,
+                         pdl, (const float*)ws1, (const int*)(rp.ntiles + 3), P,
                          (const int*)(rp.ntiles + 2), I, hq, hs),
                 "act_kernel launch");
   }
