@@ -680,7 +680,7 @@ def run_ep(args, rank, world, local):
     value = args.global_batch * args.steps / (ms * 1e-3)
     exch = {"p2p": "NVLink peer stores + epoch flags (CUDA IPC), static capacity",
             "nccl": "NCCL all-to-all, static capacity", "none": "none"}[m.exchange]
-    per_layer = {"p2p": 13, "nccl": 10, "none": 7}[m.exchange]
+    per_layer = {"p2p": 8, "nccl": 9, "none": 6}[m.exchange]
     return {
         "metric": "resident expert-parallel decode tok/s (40L, batch 64, 256 experts / N GPUs)",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,

@@ -2,6 +2,7 @@
 // the sm_100a PTX wrappers (mbarrier, TMA, tcgen05) the kernels use.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -126,6 +127,49 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     if (globaltimer_ns() - t0 > budget_ns) return false;
   }
 }
+
+// System-scope release store / acquire load of a 64-bit epoch flag (flags
+// written by another GPU over NVLink peer memory).
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// One warp: lane r < n waits until flags[r] >= want (system-scope acquire),
+// giving up after budget_ns; returns true when every flag arrived.  Callers
+// follow it with a CTA barrier so the whole CTA reads after the acquire.
+__device__ __forceinline__ bool warp_wait_epochs(const long long* flags, int n, long long want,
+                                                 unsigned long long budget_ns) {
+  const int lane = threadIdx.x & 31;
+  bool ok = true;
+  if (lane < n) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_sys(flags + lane) < want) {
+      if (globaltimer_ns() - t0 > budget_ns) { ok = false; break; }
+      __nanosleep(64);
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Expert-parallel NVLink link of one expert call: the route launch waits for
+// every source's dispatch epoch, the combine launch stores each served row
+// straight into its source's return buffer and publishes the return epoch.
+constexpr int kP2pMaxRanks = 16;
+struct P2pLink {
+  const long long* wait_flags;          // local flag_d [n_ranks]
+  const long long* epoch;               // local device epoch of this layer
+  int n_ranks, rank, cap;
+  int* err;                             // device error word
+  int wait_code;
+  unsigned long long budget_ns;
+  __nv_bfloat16* ret[kP2pMaxRanks];     // each source's return rows
+  long long* flag_r[kP2pMaxRanks];      // each source's flag_r
+  unsigned int* counter;                // local arrival counter, zero between launches
+};
 
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

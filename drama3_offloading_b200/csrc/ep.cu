@@ -94,13 +94,25 @@ __global__ void __launch_bounds__(128) ep_copy_kernel(const __nv_bfloat16* x,
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = src[v];
 }
 
-__global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ ret,
-                                  const int32_t* __restrict__ src_slot,
+// One thread per 4 columns of a token: out[t] = bf16([out[t] +] sum_k w[t,k] *
+// ret[src_slot[t,k]]), k in order.  With wait_flags set (NVLink return), one
+// warp of every CTA first waits for every serving rank's return epoch; the
+// CTA barrier after it orders all of the CTA's reads of ret after the acquire
+// (ret is written by other GPUs: no read-only-path loads).
+__global__ void ep_combine_kernel(const __nv_bfloat16* ret, const int32_t* __restrict__ src_slot,
                                   const void* __restrict__ weights, int weights_f32, int T,
                                   int topk, int H, int accumulate,
-                                  __nv_bfloat16* __restrict__ out) {
+                                  __nv_bfloat16* __restrict__ out, const long long* wait_flags,
+                                  int wait_n, const long long* wait_epoch, int* err, int code,
+                                  unsigned long long budget_ns) {
   pdl_trigger();
   pdl_wait();
+  if (wait_flags) {
+    if (threadIdx.x < 32 && !warp_wait_epochs(wait_flags, wait_n, *wait_epoch, budget_ns) &&
+        threadIdx.x == 0)
+      atomicCAS(err, 0, code);
+    __syncthreads();
+  }
   const int t = blockIdx.y;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || j >= H) return;
@@ -117,7 +129,7 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ ret,
     const float wk = weights_f32 ? static_cast<const float*>(weights)[t * topk + k]
                                  : __bfloat162float(
                                        static_cast<const __nv_bfloat16*>(weights)[t * topk + k]);
-    const uint2 raw = *reinterpret_cast<const uint2*>(ret + (size_t)slot * H + j);
+    const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(ret + (size_t)slot * H + j));
     const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[q] = fmaf(wk, __bfloat162float(b[q]), acc[q]);
@@ -160,18 +172,42 @@ int d3_ep_dispatch_pack(const void* x, const int32_t* ids, int32_t T, int32_t to
   return D3_OK;
 }
 
-int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
-                  int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
-                  int32_t accumulate, d3_stream_t stream) {
+static int ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
+                      int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
+                      int32_t accumulate, const int64_t* wait_flags, int32_t wait_n,
+                      const int64_t* epoch, int32_t* err_word, int32_t code, int64_t budget_ns,
+                      d3_stream_t stream) {
   D3_CHECK_ARG(ret && src_slot && weights && out, "d3_ep_combine: null pointer");
   D3_CHECK_ARG(T >= 1 && topk >= 1 && H >= 4 && H % 4 == 0, "bad shape");
   if (!aligned16(ret) || !aligned16(out)) return fail(D3_ERR_MISALIGNED, "ret/out not aligned");
   const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
   D3_CUDA_TRY(launch_k(ep_combine_kernel, grid, dim3(128), 0, (cudaStream_t)stream, false,
                        static_cast<const __nv_bfloat16*>(ret), src_slot, weights, weights_f32, T,
-                       topk, H, accumulate ? 1 : 0, static_cast<__nv_bfloat16*>(out)),
+                       topk, H, accumulate ? 1 : 0, static_cast<__nv_bfloat16*>(out),
+                       reinterpret_cast<const long long*>(wait_flags), (int)wait_n,
+                       reinterpret_cast<const long long*>(epoch), err_word, (int)code,
+                       (unsigned long long)budget_ns),
               "ep_combine_kernel");
   return D3_OK;
+}
+
+int d3_ep_combine(const void* ret, const int32_t* src_slot, const void* weights,
+                  int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
+                  int32_t accumulate, d3_stream_t stream) {
+  return ep_combine(ret, src_slot, weights, weights_f32, T, topk, H, out, accumulate, nullptr, 0,
+                    nullptr, nullptr, 0, 0, stream);
+}
+
+int d3_ep_combine_p2p(const void* ret, const int32_t* src_slot, const void* weights,
+                      int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
+                      int32_t accumulate, const int64_t* flag_r, int32_t n_ranks,
+                      const int64_t* epoch, int32_t* err_word, int32_t code, int64_t budget_ns,
+                      d3_stream_t stream) {
+  D3_CHECK_ARG(flag_r && epoch && err_word, "d3_ep_combine_p2p: null pointer");
+  if (n_ranks < 1 || n_ranks > 32) return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, 32]");
+  D3_CHECK_ARG(budget_ns > 0, "budget_ns must be positive");
+  return ep_combine(ret, src_slot, weights, weights_f32, T, topk, H, out, accumulate, flag_r,
+                    n_ranks, epoch, err_word, code, budget_ns, stream);
 }
 
 }  // extern "C"

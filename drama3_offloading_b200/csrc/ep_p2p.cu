@@ -11,15 +11,22 @@
 // (the same row layout the NCCL all-to-all path produces, so the expert call
 // and d3_ep_combine are shared).
 //
-// Per layer: d3_ep_dispatch_p2p (plan: stable per-destination ranks, eids
-// written straight into the destinations' recv_eid; copy: token rows stored
-// straight into the destinations' recv_x; the last CTA publishes
-// flag_d[rank] = epoch on every destination with a system-scope release) ->
-// d3_ep_wait on the local flag_d -> the expert call on recv_x ->
-// d3_ep_return_p2p (each served row stored into its source's ret, flag_r) ->
-// d3_ep_wait on flag_r -> d3_ep_combine.  The epoch is a device counter the
-// plan launch increments once per layer, so every rank agrees on it without a
-// host round trip and the whole step stays graph-capturable.
+// Per layer, three launches on each rank:
+//   d3_ep_dispatch_p2p       every pair's token row and local expert id stored
+//                            straight into its destination's recv_x/recv_eid
+//                            (stable per-destination order); the last CTA
+//                            publishes flag_d[rank] = epoch on every
+//                            destination with a system-scope release;
+//   d3_moe_fp8_forward_p2p   the expert call on recv_x (moe.cu): its route
+//                            launch first waits for every source's flag_d,
+//                            its combine launch stores each served row into
+//                            the source's ret and publishes flag_r;
+//   d3_ep_combine_p2p        waits for every serving rank's flag_r, then the
+//                            weighted sum of the returned rows (ep.cu).
+// The epoch is a device counter the dispatch launch advances once per layer,
+// so every rank agrees on it without a host round trip and the whole step
+// stays graph-capturable.  (d3_ep_return_p2p and d3_ep_wait are the unfused
+// steps, kept for callers that run their own expert computation.)
 //
 // Waits spin on system-scope acquire loads with a %globaltimer budget; on
 // expiry the kernel records an error code and returns.  Plain peer stores
@@ -35,8 +42,6 @@
 
 namespace d3 {
 
-constexpr int kP2pMaxRanks = 16;
-
 struct P2pDispatchParams {
   const int32_t* ids;
   int T, topk, n_ranks, rank, epr, cap;
@@ -51,84 +56,69 @@ struct P2pDispatchParams {
   int H;
 };
 
-__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
-  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
-  long long v;
-  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// One CTA: the layer's epoch, stable ranks per destination (pair order), the
-// destinations' recv_eid rows of this source block (unused rows -1).
-__global__ void __launch_bounds__(256) p2p_plan_kernel(P2pDispatchParams p) {
-  __shared__ int cursor[kP2pMaxRanks];
-  pdl_trigger();
-  pdl_wait();
-  const int tid = threadIdx.x, lane = tid & 31;
-  if (tid == 0) *p.epoch += 1;
-  for (int d = tid; d < p.n_ranks; d += blockDim.x) cursor[d] = 0;
-  __syncthreads();
-  const int P = p.T * p.topk;
-  if (tid < 32) {
-    for (int b0 = 0; b0 < P; b0 += 32) {
-      const int i = b0 + lane;
-      const int e = i < P ? p.ids[i] : -1;
-      const int d = (e >= 0 && e < p.n_ranks * p.epr) ? e / p.epr : -1;
-      const unsigned m = __match_any_sync(0xffffffffu, d);
-      const int leader = __ffs(m) - 1;
-      int base = 0;
-      if (lane == leader && d >= 0) {
-        base = cursor[d];
-        cursor[d] = base + __popc(m);
-      }
-      base = __shfl_sync(0xffffffffu, base, leader);
-      if (i < P) {
-        int slot = -1;
-        if (d >= 0) {
-          const int j = base + __popc(m & ((1u << lane) - 1));
-          if (j < p.cap) {
-            slot = d * p.cap + j;
-            p.recv_eid[d][p.rank * p.cap + j] = e - d * p.epr;
-          } else {
-            atomicAdd(p.overflow, 1);
-          }
-        }
-        p.src_slot[i] = slot;
-      }
-      __syncwarp();
-    }
-  }
-  __syncthreads();
-  for (int d = 0; d < p.n_ranks; ++d)
-    for (int j = cursor[d] + tid; j < p.cap; j += blockDim.x)
-      p.recv_eid[d][p.rank * p.cap + j] = -1;
-  __threadfence_system();  // the peer eid stores before anything this rank signals later
-}
-
-// One CTA per pair: its token row into the destination's recv_x; the last CTA
-// to finish publishes the epoch on every destination.
-__global__ void __launch_bounds__(128) p2p_copy_kernel(P2pDispatchParams p) {
+// One CTA per pair (and at least one per destination).  Every CTA counts the
+// pairs per destination and, for its own pair, the pairs before it with the
+// same destination (its stable rank there: pair order, as a sequential walk
+// would give), then stores the pair's token row and local expert id straight
+// into the destination's receive buffer.  CTA d < n_ranks also marks the
+// unused rows of this source's block on destination d (-1).  The last CTA to
+// finish advances the epoch and publishes it in every destination's flag_d
+// with a system-scope release, after a system fence that orders every CTA's
+// peer stores (each fenced before its arrival) first.
+__global__ void __launch_bounds__(128) p2p_dispatch_kernel(P2pDispatchParams p) {
+  __shared__ int s_cnt[kP2pMaxRanks];
+  __shared__ int s_before;
   __shared__ bool s_last;
   pdl_trigger();
   pdl_wait();
-  const int i = blockIdx.x;
-  const int slot = p.src_slot[i];
-  if (slot >= 0) {
-    const int d = slot / p.cap, j = slot - d * p.cap;
-    const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)(i / p.topk) * p.H);
-    uint4* dst = reinterpret_cast<uint4*>(p.recv_x[d] + (size_t)(p.rank * p.cap + j) * p.H);
-    for (int v = threadIdx.x; v < p.H / 8; v += blockDim.x) dst[v] = src[v];
+  const int i = blockIdx.x, tid = threadIdx.x;
+  const int P = p.T * p.topk, nexp = p.n_ranks * p.epr;
+  if (tid < kP2pMaxRanks) s_cnt[tid] = 0;
+  if (tid == 0) s_before = 0;
+  __syncthreads();
+  const int ei = i < P ? p.ids[i] : -1;
+  const int di = (ei >= 0 && ei < nexp) ? ei / p.epr : -1;
+  int before = 0;
+  for (int j = tid; j < P; j += blockDim.x) {
+    const int e = p.ids[j];
+    const int d = (e >= 0 && e < nexp) ? e / p.epr : -1;
+    if (d >= 0) {
+      atomicAdd(&s_cnt[d], 1);
+      before += (j < i && d == di);
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
+  if ((tid & 31) == 0 && before) atomicAdd(&s_before, before);
+  __syncthreads();
+  const long long epoch = *p.epoch + 1;  // the epoch this layer publishes
+  if (i < P) {
+    int slot = -1;
+    if (di >= 0) {
+      const int j = s_before;
+      if (j < p.cap) {
+        slot = di * p.cap + j;
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)(i / p.topk) * p.H);
+        uint4* dst = reinterpret_cast<uint4*>(p.recv_x[di] + (size_t)(p.rank * p.cap + j) * p.H);
+        for (int v = tid; v < p.H / 8; v += blockDim.x) dst[v] = src[v];
+        if (tid == 0) p.recv_eid[di][p.rank * p.cap + j] = ei - di * p.epr;
+      } else if (tid == 0) {
+        atomicAdd(p.overflow, 1);
+      }
+    }
+    if (tid == 0) p.src_slot[i] = slot;
+  }
+  if (i < p.n_ranks)
+    for (int j = min(s_cnt[i], p.cap) + tid; j < p.cap; j += blockDim.x)
+      p.recv_eid[i][p.rank * p.cap + j] = -1;
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  if (tid == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
-  __threadfence_system();  // every CTA's peer stores (fenced before its arrival) come first
-  if (threadIdx.x < p.n_ranks) st_release_sys(p.flag_d[threadIdx.x] + p.rank, *p.epoch);
-  if (threadIdx.x == 0) *p.counter = 0;
+  __threadfence_system();
+  if (tid < p.n_ranks) st_release_sys(p.flag_d[tid] + p.rank, epoch);
+  if (tid == 0) { *p.epoch = epoch; *p.counter = 0; }
 }
 
 struct P2pReturnParams {
@@ -163,21 +153,12 @@ __global__ void __launch_bounds__(128) p2p_return_kernel(P2pReturnParams p) {
   if (threadIdx.x == 0) *p.counter = 0;
 }
 
-// One warp: lane r waits (bounded) until flags[r] >= *epoch.
+// One warp: waits (bounded) until flags[r] >= *epoch for every rank r.
 __global__ void p2p_wait_kernel(const long long* flags, int n_ranks, const long long* epoch,
                                 int* err, int code, unsigned long long budget_ns) {
   pdl_wait();
-  const int lane = threadIdx.x;
-  bool ok = true;
-  if (lane < n_ranks) {
-    const long long want = *epoch;
-    const unsigned long long t0 = globaltimer_ns();
-    while (ld_acquire_sys(flags + lane) < want) {
-      if (globaltimer_ns() - t0 > budget_ns) { ok = false; break; }
-      __nanosleep(64);
-    }
-  }
-  if (!__all_sync(0xffffffffu, ok) && lane == 0) atomicCAS(err, 0, code);
+  const bool ok = warp_wait_epochs(flags, n_ranks, *epoch, budget_ns);
+  if (!ok && threadIdx.x == 0) atomicCAS(err, 0, code);
   __syncwarp();
   pdl_trigger();
 }
@@ -267,11 +248,9 @@ int d3_ep_dispatch_p2p(const void* x, const int32_t* ids, int32_t T, int32_t top
     p.flag_d[d] = reinterpret_cast<long long*>(peer_flag_d[d]);
   }
   cudaStream_t st = (cudaStream_t)stream;
-  // first launch of the call: an ordinary stream dependent
-  D3_CUDA_TRY(launch_k(p2p_plan_kernel, dim3(1), dim3(256), 0, st, false, p), "p2p_plan_kernel");
-  D3_CUDA_TRY(launch_k(p2p_copy_kernel, dim3((unsigned)(T * topk)), dim3(128), 0, st,
-                       pdl_enabled(), p),
-              "p2p_copy_kernel");
+  const int grid = T * topk > n_ranks ? T * topk : n_ranks;
+  D3_CUDA_TRY(launch_k(p2p_dispatch_kernel, dim3((unsigned)grid), dim3(128), 0, st, false, p),
+              "p2p_dispatch_kernel");
   return D3_OK;
 }
 

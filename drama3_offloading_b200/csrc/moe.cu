@@ -158,6 +158,9 @@ struct RouteParams {
   int mt2, nkb2, split2_min, split2_max;
   int sms;
   int nw;  // warps (chunks) of the stable sort
+  // expert-parallel NVLink link: wait for every source's dispatch epoch first
+  const long long* wait_flags; const long long* wait_epoch; int wait_n;
+  int* wait_err; int wait_code; unsigned long long wait_budget;
   // activation quantisation folded into this launch
   int fuse_quant;
   const __nv_bfloat16* x; int topk, H, Ppad;
@@ -224,6 +227,12 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   const bool lead = blockIdx.x == 0;
   pdl_trigger();
   pdl_wait();
+  if (p.wait_flags && warp == 0) {
+    // the rows and ids come from the other ranks; the barrier after the
+    // histogram reset orders every thread's reads after this acquire
+    if (!warp_wait_epochs(p.wait_flags, p.wait_n, *p.wait_epoch, p.wait_budget) && lane == 0)
+      atomicCAS(p.wait_err, 0, p.wait_code);
+  }
   for (int i = tid; i < NW * n; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const int C = route_chunk(p.P, NW);
@@ -459,8 +468,43 @@ __global__ void combine_kernel(const float* ws2, const int* split_ptr, int P, in
   const int t = blockIdx.y;
   const int j0 = (blockIdx.x * blockDim.x + (threadIdx.x & ~31)) * 4;
   if (t >= T || j0 >= H) return;
-  combine_unit(ws2, *split_ptr, P, H, inv, weights, weights_f32, t, topk, accumulate, out, j0,
-               threadIdx.x & 31);
+  combine_unit(ws2, *split_ptr, P, H, inv, weights, weights_f32, t, topk, accumulate,
+               out + (size_t)t * H, j0, threadIdx.x & 31);
+}
+
+// Expert-parallel NVLink return: one CTA per received row (t = source s *
+// cap + j); the combined row is stored straight into row (rank * cap + j) of
+// source s's return buffer (rows without a valid pair are never read there
+// and are skipped).  The last CTA to finish publishes the epoch in every
+// source's flag_r (system fence first: every CTA fenced its peer stores
+// before its arrival).
+__global__ void __launch_bounds__(256) combine_return_kernel(const float* ws2,
+                                                             const int* split_ptr, int P, int H,
+                                                             const int* inv, const void* weights,
+                                                             int weights_f32, int topk,
+                                                             P2pLink link) {
+  __shared__ bool s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool valid = false;
+  for (int k = 0; k < topk; ++k) valid |= __ldcg(inv + t * topk + k) >= 0;
+  if (valid) {
+    const int s = t / link.cap, j = t - s * link.cap;
+    __nv_bfloat16* row = link.ret[s] + (size_t)(link.rank * link.cap + j) * H;
+    const int split = *split_ptr;
+    for (int j0 = warp * 128; j0 < H; j0 += (blockDim.x >> 5) * 128)
+      combine_unit(ws2, split, P, H, inv, weights, weights_f32, t, topk, 0, row, j0, lane);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(link.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  const long long epoch = *link.epoch;
+  if (threadIdx.x < link.n_ranks) st_release_sys(link.flag_r[threadIdx.x] + link.rank, epoch);
+  if (threadIdx.x == 0) *link.counter = 0;
 }
 
 // ---------------------------------------------------------------- 3/5. GEMM
@@ -559,7 +603,8 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
                        const float* s13, const void* w2, const float* s2, int32_t n_experts,
                        int32_t H, int32_t I, void* out, int32_t accumulate, int32_t* err_word,
                        void* workspace, size_t workspace_bytes, d3_stream_t stream,
-                       const void* sw13, const void* sw2, const void* sgate) {
+                       const void* sw13, const void* sw2, const void* sgate,
+                       const P2pLink* link = nullptr) {
   D3_CHECK_ARG(x && ids && weights && w13 && s13 && w2 && s2 && out && err_word,
                "d3_moe_fp8_forward: null pointer");
   D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
@@ -592,7 +637,7 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
                   "multiples of 512); run it separately for larger batches",
                   kGemvMaxPairsDefault);
   }
-  if (sw13 || gemv_supported(P, topk, H, I)) {
+  if (sw13 || (!link && gemv_supported(P, topk, H, I))) {
     // decode-sized batch: two CUDA-core launches; h (and the shared expert's
     // h and gate) live where gemm1's partials would (split1_max * P * 2I
     // floats >= P * I + T * I + T)
@@ -633,6 +678,10 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   rp.fuse_quant = P <= kFusedQuantMaxPairs ? 1 : 0;
   rp.x = static_cast<const __nv_bfloat16*>(x);
   rp.topk = topk; rp.H = H; rp.Ppad = pl.Ppad; rp.xq = xq; rp.xs = xs;
+  if (link) {
+    rp.wait_flags = link->wait_flags; rp.wait_epoch = link->epoch; rp.wait_n = link->n_ranks;
+    rp.wait_err = link->err; rp.wait_code = link->wait_code; rp.wait_budget = link->budget_ns;
+  }
   const bool pdl = pdl_enabled();
   // shared memory: cnt, off, tile prefix [n] + sorted [P] (fused) + NW chunk
   // histograms of n ints, as many chunks (<= 32, <= the 32-pair batches) as
@@ -701,7 +750,12 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   rc = pl.BN == 16 ? launch_gemm<16, 2>(tw2, tx2, g2, pl.maxt2, st)
                    : launch_gemm<64, 2>(tw2, tx2, g2, pl.maxt2, st);
   if (rc) return rc;
-  {
+  if (link) {
+    D3_CUDA_TRY(launch_k(combine_return_kernel, dim3((unsigned)T), dim3(256), 0, st, pdl,
+                         (const float*)ws2, (const int*)(rp.ntiles + 4), P, H, (const int*)rp.inv,
+                         weights, weights_f32, topk, *link),
+                "combine_return_kernel launch");
+  } else {
     const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
     D3_CUDA_TRY(launch_k(combine_kernel, grid, dim3(128), 0, st, pdl, (const float*)ws2,
                          (const int*)(rp.ntiles + 4), P, H, (const int*)rp.inv, weights,
@@ -735,6 +789,38 @@ int d3_moe_fp8_forward_shared(const void* x, const void* ids, int32_t ids_bytes,
   return moe_forward(x, ids, ids_bytes, weights, weights_f32, T, topk, w13, s13, w2, s2,
                      n_experts, H, I, out, accumulate, err_word, workspace, workspace_bytes,
                      stream, shared_w13, shared_w2, shared_gate);
+}
+
+int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,
+                           const void* weights, int32_t weights_f32, int32_t T, int32_t topk,
+                           const void* w13, const float* s13, const void* w2, const float* s2,
+                           int32_t n_experts, int32_t H, int32_t I, int32_t* err_word,
+                           void* workspace, size_t workspace_bytes, const int64_t* wait_flags,
+                           const int64_t* epoch, int32_t n_ranks, int32_t rank, int32_t cap,
+                           void* const* peer_ret, int64_t* const* peer_flag_r, uint32_t* counter,
+                           int32_t wait_code, int64_t budget_ns, d3_stream_t stream) {
+  D3_CHECK_ARG(wait_flags && epoch && peer_ret && peer_flag_r && counter && err_word,
+               "d3_moe_fp8_forward_p2p: null pointer");
+  if (n_ranks < 1 || n_ranks > kP2pMaxRanks)
+    return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, %d]", kP2pMaxRanks);
+  D3_CHECK_ARG(rank >= 0 && rank < n_ranks && cap >= 1 && (long)n_ranks * cap == T,
+               "rank out of range or T != n_ranks * cap");
+  D3_CHECK_ARG(budget_ns > 0, "budget_ns must be positive");
+  P2pLink link{};
+  link.wait_flags = reinterpret_cast<const long long*>(wait_flags);
+  link.epoch = reinterpret_cast<const long long*>(epoch);
+  link.n_ranks = n_ranks; link.rank = rank; link.cap = cap;
+  link.err = err_word; link.wait_code = wait_code; link.budget_ns = (unsigned long long)budget_ns;
+  link.counter = counter;
+  for (int s = 0; s < n_ranks; ++s) {
+    D3_CHECK_ARG(peer_ret[s] && peer_flag_r[s], "d3_moe_fp8_forward_p2p: null peer pointer");
+    if (!aligned16(peer_ret[s])) return fail(D3_ERR_MISALIGNED, "peer ret must be 16-byte aligned");
+    link.ret[s] = static_cast<__nv_bfloat16*>(peer_ret[s]);
+    link.flag_r[s] = reinterpret_cast<long long*>(peer_flag_r[s]);
+  }
+  return moe_forward(x, ids, ids_bytes, weights, weights_f32, T, topk, w13, s13, w2, s2,
+                     n_experts, H, I, peer_ret[0], 0, err_word, workspace, workspace_bytes, stream,
+                     nullptr, nullptr, nullptr, &link);
 }
 
 }  // extern "C"

@@ -63,15 +63,16 @@ __device__ __forceinline__ void act_unit(const float* ws1, int split, int P, int
 }
 
 // ws2: [split][P][H] fp32 partials; inv[t*topk+k] = sorted row of pair (t,k)
-// or -1; columns [j0, j0 + 128) of token t.
+// or -1; columns [j0, j0 + 128) of token t into out_row (token t's output row,
+// local or a peer's).
 __device__ __forceinline__ void combine_unit(const float* ws2, int split, int P, int H,
                                              const int* inv, const void* weights, int weights_f32,
                                              int t, int topk, int accumulate,
-                                             __nv_bfloat16* out, int j0, int lane) {
+                                             __nv_bfloat16* out_row, int j0, int lane) {
   const int j = j0 + lane * 4;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (accumulate) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(out + (size_t)t * H + j);
+    const uint2 raw = *reinterpret_cast<const uint2*>(out_row + j);
     const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[q] = __bfloat162float(b[q]);
@@ -93,7 +94,7 @@ __device__ __forceinline__ void combine_unit(const float* ws2, int split, int P,
   __nv_bfloat16 o[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) o[q] = __float2bfloat16_rn(acc[q]);
-  *reinterpret_cast<uint2*>(out + (size_t)t * H + j) = *reinterpret_cast<uint2*>(o);
+  *reinterpret_cast<uint2*>(out_row + j) = *reinterpret_cast<uint2*>(o);
 }
 
 }  // namespace d3

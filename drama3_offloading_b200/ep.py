@@ -182,30 +182,33 @@ class ExpertParallelMoE:
     WAIT_BUDGET_NS = 2_000_000_000
 
     def _layer_p2p(self, l, ids, w, st, gemm_events) -> None:
-        """The same layer with the exchange over NVLink peer stores."""
+        """The same layer with the exchange over NVLink peer stores, in three C
+        calls: the dispatch stores the rows into the peers; the expert call
+        waits for every source's rows (in its route launch) and stores each
+        served row back into its source (in its combine launch); the combine
+        waits for every serving rank's rows."""
         x = self.p2p
         err = moe.error_word(self.device)
         _lib.call("d3_ep_dispatch_p2p", _lib.ptr(self.h), _lib.ptr(ids), self.T, self.k, self.H,
                   self.world, self.rank, self.epr, self.cap, x.peer["recv_x"],
                   x.peer["recv_eid"], x.peer["flag_d"], _lib.ptr(self.src_slot),
                   _lib.ptr(self.overflow), _lib.ptr(x.epoch), _lib.ptr(x.counters), st)
-        _lib.call("d3_ep_wait", _lib.ptr(x.flag_d), self.world, _lib.ptr(x.epoch),
-                  _lib.ptr(err), 31, self.WAIT_BUDGET_NS, st)
         if gemm_events is not None:
             e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
             e0.record()
-        moe.fp8_moe_forward(x.recv_x, x.recv_eid.view(-1, 1), self.ones, w.w13_weight,
-                            w.w13_scale_inv, w.w2_weight, w.w2_scale_inv, out=self.y)
+        moe.fp8_moe_forward_p2p(x.recv_x, x.recv_eid.view(-1, 1), self.ones, w.w13_weight,
+                                w.w13_scale_inv, w.w2_weight, w.w2_scale_inv,
+                                wait_flags=x.flag_d, epoch=x.epoch, n_ranks=self.world,
+                                rank=self.rank, cap=self.cap, peer_ret=x.peer["ret"],
+                                peer_flag_r=x.peer["flag_r"], counter=x.counters[1:],
+                                wait_code=31, budget_ns=self.WAIT_BUDGET_NS)
         if gemm_events is not None:
             e1.record()
             gemm_events.append((e0, e1))
-        _lib.call("d3_ep_return_p2p", _lib.ptr(self.y), _lib.ptr(x.recv_eid), self.world,
-                  self.rank, self.cap, self.H, x.peer["ret"], x.peer["flag_r"],
-                  _lib.ptr(x.epoch), _lib.ptr(x.counters[1:]), st)
-        _lib.call("d3_ep_wait", _lib.ptr(x.flag_r), self.world, _lib.ptr(x.epoch),
-                  _lib.ptr(err), 32, self.WAIT_BUDGET_NS, st)
-        _lib.call("d3_ep_combine", _lib.ptr(x.ret), _lib.ptr(self.src_slot),
-                  _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(self.h), 1, st)
+        _lib.call("d3_ep_combine_p2p", _lib.ptr(x.ret), _lib.ptr(self.src_slot),
+                  _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(self.h), 1,
+                  _lib.ptr(x.flag_r), self.world, _lib.ptr(x.epoch), _lib.ptr(err), 32,
+                  self.WAIT_BUDGET_NS, st)
 
     def close(self) -> None:
         """Unmap the peers' exchange buffers (after the last step, on every rank)."""

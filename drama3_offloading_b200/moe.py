@@ -167,3 +167,44 @@ def fp8_moe_forward(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
               1 if accumulate else 0, _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(),
               _lib.stream_ptr(stream))
     return out
+
+
+def fp8_moe_forward_p2p(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                        w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor,
+                        s2: torch.Tensor, *, wait_flags: torch.Tensor, epoch: torch.Tensor,
+                        n_ranks: int, rank: int, cap: int, peer_ret, peer_flag_r,
+                        counter: torch.Tensor, wait_code: int, budget_ns: int,
+                        stream=None) -> None:
+    """The expert call of one expert-parallel layer over NVLink peer memory
+    (``d3_moe_fp8_forward_p2p``): waits for every source's dispatch epoch in
+    ``wait_flags``, runs the routed experts on the received rows ``x``
+    ([n_ranks * cap, H] bf16, ids = local expert ids, -1 for unused rows) and
+    stores each served row straight into its source's return buffer
+    (``peer_ret``: ctypes array of n_ranks device pointers), publishing the
+    epoch in every source's flag_r (``peer_flag_r``).  Nothing is returned
+    locally."""
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise TypeError("x must be contiguous bf16")
+    T, H = x.shape
+    ids = ids.reshape(T, -1)
+    topk = ids.shape[1]
+    if ids.dtype not in (torch.int32, torch.int64) or not ids.is_contiguous():
+        raise TypeError("ids must be contiguous int32/int64")
+    weights = weights.reshape(T, topk)
+    if weights.dtype not in (torch.float32, torch.bfloat16) or not weights.is_contiguous():
+        raise TypeError("weights must be contiguous f32/bf16")
+    n, two_i, h2 = w13.shape
+    if h2 != H or w2.shape[0] != n or w2.shape[1] != H:
+        raise ValueError("weight shapes do not match x")
+    I = two_i // 2
+    dev = x.device
+    need = workspace_bytes(T, topk, n, H, I)
+    if need == 0:
+        raise ValueError(f"unsupported MoE shape T={T} topk={topk} n={n} H={H} I={I}")
+    ws = _workspace(dev, need, "moe")
+    wf = 1 if weights.dtype == torch.float32 else 0
+    _lib.call("d3_moe_fp8_forward_p2p", _lib.ptr(x), _lib.ptr(ids), ids.element_size(),
+              _lib.ptr(weights), wf, T, topk, _lib.ptr(w13), _lib.ptr(s13), _lib.ptr(w2),
+              _lib.ptr(s2), n, H, I, _lib.ptr(error_word(dev)), _lib.ptr(ws), ws.numel(),
+              _lib.ptr(wait_flags), _lib.ptr(epoch), n_ranks, rank, cap, peer_ret, peer_flag_r,
+              _lib.ptr(counter), wait_code, budget_ns, _lib.stream_ptr(stream))

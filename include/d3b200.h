@@ -305,6 +305,36 @@ D3_API int d3_ep_return_p2p(const void* y, const int32_t* recv_eid, int32_t n_ra
 D3_API int d3_ep_wait(const int64_t* flags, int32_t n_ranks, const int64_t* epoch,
                       int32_t* err_word, int32_t code, int64_t budget_ns, d3_stream_t stream);
 
+/* The expert call of one expert-parallel layer with the NVLink exchange folded
+ * into its first and last launches: d3_moe_fp8_forward over the received rows
+ * (x = recv_x [T = n_ranks*cap, H], ids = recv_eid, topk normally 1), whose
+ * route launch first waits (bounded, budget_ns; on expiry *err_word =
+ * wait_code) until wait_flags[r] >= *epoch for every rank r, and whose combine
+ * launch stores each served row t = s*cap + j straight into row rank*cap + j
+ * of source s's return buffer (peer_ret[s]), then publishes
+ * peer_flag_r[s][rank] = *epoch on every source.  counter: a device uint32,
+ * zero between calls.  Always the tensor-core path; no accumulate.  Replaces
+ * d3_ep_wait + d3_moe_fp8_forward + d3_ep_return_p2p.  No counterpart in the
+ * reference. */
+D3_API int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,
+                                  const void* weights, int32_t weights_f32, int32_t T,
+                                  int32_t topk, const void* w13, const float* s13, const void* w2,
+                                  const float* s2, int32_t n_experts, int32_t H, int32_t I,
+                                  int32_t* err_word, void* workspace, size_t workspace_bytes,
+                                  const int64_t* wait_flags, const int64_t* epoch,
+                                  int32_t n_ranks, int32_t rank, int32_t cap,
+                                  void* const* peer_ret, int64_t* const* peer_flag_r,
+                                  uint32_t* counter, int32_t wait_code, int64_t budget_ns,
+                                  d3_stream_t stream);
+
+/* d3_ep_combine after a bounded wait (as d3_ep_wait) until flag_r[r] >= *epoch
+ * for every serving rank r: replaces d3_ep_wait + d3_ep_combine. */
+D3_API int d3_ep_combine_p2p(const void* ret, const int32_t* src_slot, const void* weights,
+                             int32_t weights_f32, int32_t T, int32_t topk, int32_t H, void* out,
+                             int32_t accumulate, const int64_t* flag_r, int32_t n_ranks,
+                             const int64_t* epoch, int32_t* err_word, int32_t code,
+                             int64_t budget_ns, d3_stream_t stream);
+
 /* ---------------------------------------------------------------- routing census / trace */
 
 /* counts[e] += occurrences of expert e among the rows*k ids (int32 or int64,
