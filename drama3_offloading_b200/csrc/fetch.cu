@@ -27,6 +27,7 @@
 //    (griddepcontrol), so its CTAs are resident before the allocator ends.
 
 #include "d3_common.cuh"
+#include "fetch_flat.cuh"
 
 #include <stdlib.h>
 #include <string.h>
@@ -96,20 +97,6 @@ __global__ void __launch_bounds__(256) fetch_jobs_kernel(const uint4* __restrict
   for (; i < vec_per_expert; i += stride) d[i] = ld_stream_u4(s + i);
 }
 
-struct FetchParams {
-  const uint4* host[D3_MAX_BUFFERS];
-  uint4* cache[D3_MAX_BUFFERS];
-  int64_t vecs[D3_MAX_BUFFERS];   // 16-byte vectors per expert, per buffer
-  int64_t vec_total;              // sum over buffers
-  int32_t nbuf;
-  const int32_t* fetch_slot;
-  const int32_t* fetch_expert;
-  const int32_t* nmiss;
-};
-
-constexpr int kFetchThreads = 256;
-constexpr int kFetchUnroll = 4;
-
 // Flat multi-buffer fetch: the byte range of job j / buffer b / vector v is
 // linearised as j*vec_total + (prefix_b + v); CTAs stride over chunks of
 // kFetchThreads*kFetchUnroll vectors (16 KiB).
@@ -162,6 +149,8 @@ struct ResolveParams {
   int32_t* nmiss;
   int64_t* counters;
   int64_t expert_bytes;
+  int64_t* zero;       // [nzero] cleared by this launch (the overlap launch's counters)
+  int32_t nzero;
 };
 
 __device__ __forceinline__ int32_t load_id(const void* ids, int bytes, int i) {
@@ -224,6 +213,7 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
     if (lfu) { s_freq[c] = p.freq[c]; s_ins[c] = p.ins[c]; }
   }
   const int64_t step = *p.step + 1;
+  for (int i = lane; i < p.nzero; i += 32) p.zero[i] = 0;
   __syncwarp();
   int out_lo = -1, out_hi = -1;
   int nmiss = 0, hits = 0;
@@ -503,6 +493,39 @@ static int launch_fetch(const FetchParams& fp, int fetch_ctas, cudaStream_t st, 
   return D3_OK;
 }
 
+int resolve_for_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
+                      int64_t* zero, int32_t nzero, cudaStream_t st, FetchParams* fp,
+                      int64_t* expert_bytes) {
+  D3_CHECK_ARG(L && ids, "d3_resolve_fetch: null pointer");
+  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
+  D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
+  D3_CHECK_ARG(L->num_experts >= 1, "num_experts must be >= 1");
+  if (L->capacity < 1 || L->capacity > 8192)
+    return fail(D3_ERR_TOO_LARGE, "capacity must be in [1, 8192] (got %d)", L->capacity);
+  D3_CHECK_ARG(L->policy == D3_POLICY_LRU || L->policy == D3_POLICY_LFU, "unknown policy %d",
+               L->policy);
+  D3_CHECK_ARG(L->nbuf >= 1 && L->nbuf <= D3_MAX_BUFFERS, "nbuf must be in [1, %d]",
+               D3_MAX_BUFFERS);
+  D3_CHECK_ARG(L->slot_of && L->slot_expert && L->stamp && L->step && L->out_slot &&
+                   L->fetch_slot && L->fetch_expert && L->nmiss,
+               "d3_resolve_fetch: null table pointer");
+  if (L->policy == D3_POLICY_LFU)
+    D3_CHECK_ARG(L->freq && L->ins, "LFU needs freq and ins tables");
+  D3_CHECK_ARG(nzero >= 0 && nzero <= 64 && (nzero == 0 || zero), "zero list out of range");
+  *fp = FetchParams{};
+  int rc = make_fetch_params(L, fp, expert_bytes);
+  if (rc) return rc;
+  ResolveParams p{};
+  p.ids = ids; p.ids_bytes = ids_bytes; p.k = k; p.num_experts = L->num_experts;
+  p.capacity = L->capacity; p.policy = L->policy;
+  p.slot_of = L->slot_of; p.slot_expert = L->slot_expert; p.stamp = L->stamp; p.step = L->step;
+  p.freq = L->freq; p.ins = L->ins;
+  p.out_slot = L->out_slot; p.fetch_slot = L->fetch_slot; p.fetch_expert = L->fetch_expert;
+  p.nmiss = L->nmiss; p.counters = L->counters; p.expert_bytes = *expert_bytes;
+  p.zero = zero; p.nzero = nzero;
+  return launch_resolve(p, st);
+}
+
 }  // namespace d3
 
 using namespace d3;
@@ -606,36 +629,11 @@ int d3_resolve_slots(const void* ids, int32_t ids_bytes, int32_t k, int32_t* slo
 
 int d3_resolve_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
                      int32_t fetch_ctas, d3_stream_t stream) {
-  D3_CHECK_ARG(L && ids, "d3_resolve_fetch: null pointer");
-  D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
-  D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
-  D3_CHECK_ARG(L->num_experts >= 1, "num_experts must be >= 1");
-  if (L->capacity < 1 || L->capacity > 8192)
-    return fail(D3_ERR_TOO_LARGE, "capacity must be in [1, 8192] (got %d)", L->capacity);
-  D3_CHECK_ARG(L->policy == D3_POLICY_LRU || L->policy == D3_POLICY_LFU, "unknown policy %d",
-               L->policy);
-  D3_CHECK_ARG(L->nbuf >= 1 && L->nbuf <= D3_MAX_BUFFERS, "nbuf must be in [1, %d]",
-               D3_MAX_BUFFERS);
-  D3_CHECK_ARG(L->slot_of && L->slot_expert && L->stamp && L->step && L->out_slot &&
-                   L->fetch_slot && L->fetch_expert && L->nmiss,
-               "d3_resolve_fetch: null table pointer");
-  if (L->policy == D3_POLICY_LFU)
-    D3_CHECK_ARG(L->freq && L->ins, "LFU needs freq and ins tables");
   D3_CHECK_ARG(fetch_ctas >= 0 && fetch_ctas <= 65535, "fetch_ctas out of range");
   FetchParams fp{};
   int64_t expert_bytes = 0;
-  int rc = make_fetch_params(L, &fp, &expert_bytes);
-  if (rc) return rc;
-
-  ResolveParams p{};
-  p.ids = ids; p.ids_bytes = ids_bytes; p.k = k; p.num_experts = L->num_experts;
-  p.capacity = L->capacity; p.policy = L->policy;
-  p.slot_of = L->slot_of; p.slot_expert = L->slot_expert; p.stamp = L->stamp; p.step = L->step;
-  p.freq = L->freq; p.ins = L->ins;
-  p.out_slot = L->out_slot; p.fetch_slot = L->fetch_slot; p.fetch_expert = L->fetch_expert;
-  p.nmiss = L->nmiss; p.counters = L->counters; p.expert_bytes = expert_bytes;
   cudaStream_t st = (cudaStream_t)stream;
-  rc = launch_resolve(p, st);
+  const int rc = resolve_for_fetch(L, ids, ids_bytes, k, nullptr, 0, st, &fp, &expert_bytes);
   if (rc) return rc;
   return launch_fetch(fp, fetch_ctas, st, pdl_enabled());
 }

@@ -32,6 +32,7 @@
 // once per N tile; K-splits spread a small batch's few experts over all SMs.
 #include "d3_common.cuh"
 #include "gemm_sm100.cuh"
+#include "fetch_flat.cuh"
 #include "moe_epilogue.cuh"
 #include "moe_gemv.cuh"
 
@@ -554,6 +555,8 @@ static cudaError_t launch_gemv2(const GemvParams& gp, dim3 grid, int rpw, size_t
   return launch_k(moe_gemv2_kernel<C2>, grid, dim3(kGemvThreads), smem, st, pdl, gp, rpw);
 }
 
+static int run_gemv2(const GemvParams& gp, cudaStream_t st, bool pdl);
+
 static int run_gemv(const GemvParams& gp, cudaStream_t st) {
   const int sms = num_sms();
   const long units1 = (long)gp.T * gp.topk * gp.I;  // one warp each
@@ -567,11 +570,16 @@ static int run_gemv(const GemvParams& gp, cudaStream_t st) {
     default: e = launch_gemv13<8>(gp, (int)ctas1, st); break;
   }
   D3_CUDA_TRY(e, "moe_gemv13_kernel launch");
+  return run_gemv2(gp, st, pdl_enabled());
+}
+
+static int run_gemv2(const GemvParams& gp, cudaStream_t st, bool pdl) {
+  const int sms = num_sms();
+  cudaError_t e;
   int rpw = 1;  // output rows per warp: more once the grid would exceed ~4 CTAs per SM
   while (rpw < 4 && (long)gp.T * gp.H / (kGemvRowsPerCta * rpw) > 4L * sms) rpw *= 2;
   const dim3 grid2((unsigned)(gp.H / (kGemvRowsPerCta * rpw)), (unsigned)gp.T);
   const size_t smem = gemv2_smem(gp.topk + (gp.sw13 ? 1 : 0), gp.I);
-  const bool pdl = pdl_enabled();
   switch (gp.I / 512) {
     case 1: e = launch_gemv2<1>(gp, grid2, rpw, smem, st, pdl); break;
     case 2: e = launch_gemv2<2>(gp, grid2, rpw, smem, st, pdl); break;
@@ -579,6 +587,135 @@ static int run_gemv(const GemvParams& gp, cudaStream_t st) {
   }
   D3_CUDA_TRY(e, "moe_gemv2_kernel launch");
   return D3_OK;
+}
+
+// ---------------------------------------------------------------- fetch + gate/up overlap
+//
+// Decode with offloaded experts: ONE launch both fetches the layer's missed
+// experts from pinned host memory and runs the gate/up units.  CTAs
+// [0, fetch_ctas) fetch -- first the W13 and S13 bytes of every job (job
+// after job), then the rest (W2, S2) -- and count, per job, the W13/S13
+// vectors that have landed (one fence + atomic per job per CTA, when the CTA
+// leaves that job's range).  The other CTAs run the gate/up units of the
+// resident experts and of the shared expert at once, then the units of each
+// fetched expert after a bounded wait until its job's count is complete: a
+// per-slot in-flight state (queued -> landed) instead of a launch boundary.
+// The down projection (gemv2) follows as its own launch and reads W2 only
+// after griddepcontrol.wait (this launch writes W2).
+struct FetchOverlapParams {
+  unsigned long long* done;   // [64] W13+S13 vectors landed per job (zeroed by the resolve launch)
+  int fetch_ctas;
+  uint32_t early_mask;        // buffers the gate/up units read (W13, S13)
+  int64_t vecA;               // vectors per job in those buffers
+  int* err;
+  int err_code;
+  unsigned long long budget_ns;
+};
+
+__device__ __forceinline__ void overlap_vec(const FetchParams& f, uint32_t mask, bool early,
+                                            int64_t r, int64_t e, int64_t s, const uint4** src,
+                                            uint4** dst) {
+  for (int b = 0; b < f.nbuf; ++b) {
+    if ((((mask >> b) & 1u) != 0u) != early) continue;
+    if (r < f.vecs[b]) {
+      *src = f.host[b] + e * f.vecs[b] + r;
+      *dst = f.cache[b] + s * f.vecs[b] + r;
+      return;
+    }
+    r -= f.vecs[b];
+  }
+}
+
+__device__ void overlap_fetch(const FetchParams& f, const FetchOverlapParams& o, int nm) {
+  const int64_t vecA = o.vecA, vecB = f.vec_total - vecA;
+  const int64_t totA = (int64_t)nm * vecA, total = (int64_t)nm * f.vec_total;
+  constexpr int64_t kChunk = (int64_t)kFetchThreads * kFetchUnroll;
+  const int64_t stride = (int64_t)o.fetch_ctas * kChunk;
+  int pj = -1;                 // job whose landed vectors this CTA still has to publish
+  unsigned long long pc = 0;
+  // (uniform over the CTA: every thread runs the same chunk sequence)
+  auto flush = [&]() {
+    __syncthreads();           // every thread's stores of the counted chunks are issued
+    if (threadIdx.x == 0) {
+      __threadfence();         // ... and visible GPU-wide before the count moves
+      atomicAdd(o.done + pj, pc);
+    }
+    pj = -1;
+    pc = 0;
+  };
+  for (int64_t base = (int64_t)blockIdx.x * kChunk; base < total; base += stride) {
+    uint4 v[kFetchUnroll];
+    uint4* dptr[kFetchUnroll];
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u) {
+      const int64_t g = base + (int64_t)u * kFetchThreads + threadIdx.x;
+      dptr[u] = nullptr;
+      if (g < total) {
+        const bool early = g < totA;
+        const int64_t gg = early ? g : g - totA, per = early ? vecA : vecB;
+        const int64_t j = gg / per, r = gg - j * per;
+        const uint4* src = nullptr;
+        uint4* dst = nullptr;
+        overlap_vec(f, o.early_mask, early, r, __ldcg(f.fetch_expert + j),
+                    __ldcg(f.fetch_slot + j), &src, &dst);
+        v[u] = ld_stream_u4(src);
+        dptr[u] = dst;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kFetchUnroll; ++u)
+      if (dptr[u]) *dptr[u] = v[u];
+    if (base < totA) {
+      const int64_t hi = base + kChunk < totA ? base + kChunk : totA;
+      const int j0 = (int)(base / vecA), j1 = (int)((hi - 1) / vecA);
+      for (int j = j0; j <= j1; ++j) {
+        const int64_t lo_j = base > (int64_t)j * vecA ? base : (int64_t)j * vecA;
+        const int64_t hi_j = hi < (int64_t)(j + 1) * vecA ? hi : (int64_t)(j + 1) * vecA;
+        if (pj != j) {
+          if (pj >= 0) flush();
+          pj = j;
+        }
+        pc += (unsigned long long)(hi_j - lo_j);
+        if (j < j1) flush();   // this CTA's later chunks all lie past job j
+      }
+      const int64_t next = base + stride;
+      if (pj >= 0 && (next >= totA || next >= (int64_t)(pj + 1) * vecA)) flush();
+    }
+  }
+  if (pj >= 0) flush();
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) fetch_gemv13_kernel(FetchParams f, GemvParams p,
+                                                                    FetchOverlapParams o) {
+  __shared__ int s_job[64];
+  pdl_wait();     // the allocator's job table (and cleared counters) are complete
+  pdl_trigger();  // gemv2 reads nothing this launch writes before its own wait
+  const int nm = *f.nmiss;
+  if ((int)blockIdx.x < o.fetch_ctas) {
+    if (nm > 0) overlap_fetch(f, o, nm);
+    return;
+  }
+  const int P = p.T * p.topk;  // <= 64
+  if ((int)threadIdx.x < P) {
+    const int s = gemv_pair_id(p.ids, p.ids_bytes, threadIdx.x, p.n);
+    int job = -1;
+    for (int j = 0; j < nm; ++j)
+      if (s >= 0 && __ldcg(f.fetch_slot + j) == s) job = j;
+    s_job[threadIdx.x] = job;
+  }
+  __syncthreads();
+  const GemvOverlap ov{s_job, o.done, (unsigned long long)o.vecA, o.err, o.err_code, o.budget_ns};
+  const long gw = ((long)(blockIdx.x - o.fetch_ctas) * blockDim.x + threadIdx.x) >> 5;
+  const long nw = ((long)(gridDim.x - o.fetch_ctas) * blockDim.x) >> 5;
+  gemv13_units<CPL>(p, gw, nw, &ov);
+}
+
+constexpr uint64_t kOverlapWaitBudgetNs = 2000000000ull;
+constexpr int kOverlapFetchCtas = 64;   // measured: 16 -> 80, 32 -> 102, 64 / 148 -> 103.7 tok/s
+
+static size_t overlap_workspace(int k, int I) {
+  return al(64 * sizeof(unsigned long long)) + al(sizeof(float) * ((size_t)k * I + I + 1));
 }
 
 }  // namespace d3
@@ -656,6 +793,7 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
     gp.sgate = static_cast<const __nv_bfloat16*>(sgate);
     gp.hs = gp.h + (size_t)P * I;
     gp.gs = gp.hs + (size_t)T * I;
+    gp.w2_early = 1;
     return run_gemv(gp, st);
   }
 
@@ -789,6 +927,89 @@ int d3_moe_fp8_forward_shared(const void* x, const void* ids, int32_t ids_bytes,
   return moe_forward(x, ids, ids_bytes, weights, weights_f32, T, topk, w13, s13, w2, s2,
                      n_experts, H, I, out, accumulate, err_word, workspace, workspace_bytes,
                      stream, shared_w13, shared_w2, shared_gate);
+}
+
+size_t d3_resolve_fetch_moe_workspace_size(int32_t k, int32_t H, int32_t I) {
+  if (k < 1 || k > 64 || H < 512 || I < 512) return 0;
+  return overlap_workspace(k, I);
+}
+
+int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
+                         const void* x, const void* weights, int32_t weights_f32, int32_t H,
+                         int32_t I, const void* shared_w13, const void* shared_w2,
+                         const void* shared_gate, void* out, int32_t accumulate,
+                         int32_t* err_word, void* workspace, size_t workspace_bytes,
+                         int32_t fetch_ctas, int32_t stages, d3_stream_t stream) {
+  D3_CHECK_ARG(L && ids && x && weights && out && err_word, "d3_resolve_fetch_moe: null pointer");
+  D3_CHECK_ARG(stages >= 1 && stages <= 3, "stages must be 1, 2 or 3");
+  D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
+  if (!gemv_shapes_ok(k, H, I))
+    return fail(D3_ERR_UNSUPPORTED, "H and I must be 512 x {1,2,4,8} / {1,2,4}");
+  D3_CHECK_ARG(L->nbuf == 4, "the layer cache must hold the 4 buffers w13, w2, s13, s2");
+  const int64_t b13 = 2LL * I * H, b2 = (int64_t)H * I;
+  const int64_t bs13 = (2LL * I / 128) * (H / 128) * 4, bs2 = ((int64_t)H / 128) * (I / 128) * 4;
+  if (L->bytes[0] != b13 || L->bytes[1] != b2 || L->bytes[2] != bs13 || L->bytes[3] != bs2)
+    return fail(D3_ERR_INVALID_ARG, "buffer sizes do not match H=%d I=%d", H, I);
+  if (L->capacity < k)
+    return fail(D3_ERR_UNSUPPORTED, "capacity %d < k %d (a slot could be filled twice)",
+                L->capacity, k);
+  D3_CHECK_ARG(fetch_ctas >= 0 && fetch_ctas <= 1024, "fetch_ctas out of range");
+  if (shared_w13 || shared_w2) D3_CHECK_ARG(shared_w13 && shared_w2, "shared expert incomplete");
+  if (!aligned16(x) || !aligned16(out) ||
+      (shared_w13 && (!aligned16(shared_w13) || !aligned16(shared_w2))) ||
+      (shared_gate && !aligned16(shared_gate)))
+    return fail(D3_ERR_MISALIGNED, "x, out and the shared expert weights must be 16-byte aligned");
+  if (!workspace || workspace_bytes < overlap_workspace(k, I))
+    return fail(D3_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", overlap_workspace(k, I),
+                workspace_bytes);
+  if (!aligned16(workspace)) return fail(D3_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  auto* done = reinterpret_cast<unsigned long long*>(ws);
+  cudaStream_t st = (cudaStream_t)stream;
+  GemvParams gp{};
+  gp.x = static_cast<const __nv_bfloat16*>(x);
+  gp.ids = L->out_slot; gp.ids_bytes = 4;
+  gp.weights = weights; gp.weights_f32 = weights_f32 ? 1 : 0;
+  gp.T = 1; gp.topk = k; gp.n = L->capacity; gp.H = H; gp.I = I;
+  gp.accumulate = accumulate ? 1 : 0;
+  gp.w13 = static_cast<const uint8_t*>(L->cache[0]);
+  gp.w2 = static_cast<const uint8_t*>(L->cache[1]);
+  gp.s13 = static_cast<const float*>(L->cache[2]);
+  gp.s2 = static_cast<const float*>(L->cache[3]);
+  gp.h = reinterpret_cast<float*>(ws + al(64 * sizeof(unsigned long long)));
+  gp.hs = gp.h + (size_t)k * I;
+  gp.gs = gp.hs + I;
+  gp.out = static_cast<__nv_bfloat16*>(out);
+  gp.sw13 = static_cast<const __nv_bfloat16*>(shared_w13);
+  gp.sw2 = static_cast<const __nv_bfloat16*>(shared_w2);
+  gp.sgate = static_cast<const __nv_bfloat16*>(shared_gate);
+  gp.w2_early = 0;
+  if (!(stages & 1)) return run_gemv2(gp, st, false);  // a call's first launch: no PDL
+  FetchParams fp{};
+  int64_t expert_bytes = 0;
+  int rc = resolve_for_fetch(L, ids, ids_bytes, k, reinterpret_cast<int64_t*>(done), 64, st, &fp,
+                             &expert_bytes);
+  if (rc) return rc;
+  FetchOverlapParams o{};
+  o.done = done;
+  // fetch CTAs, then the rest of one resident wave (2 CTAs per SM) runs the
+  // gate/up units
+  o.fetch_ctas = fetch_ctas > 0 ? fetch_ctas : kOverlapFetchCtas;
+  if (o.fetch_ctas > num_sms()) o.fetch_ctas = num_sms();
+  o.early_mask = (1u << 0) | (1u << 2);
+  o.vecA = (b13 + bs13) / 16;
+  o.err = err_word; o.err_code = 41; o.budget_ns = kOverlapWaitBudgetNs;
+  const int grid = 2 * num_sms();
+  cudaError_t e;
+  const bool pdl = pdl_enabled();
+  switch (H / 512) {
+    case 1: e = launch_k(fetch_gemv13_kernel<1>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
+    case 2: e = launch_k(fetch_gemv13_kernel<2>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
+    case 4: e = launch_k(fetch_gemv13_kernel<4>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
+    default: e = launch_k(fetch_gemv13_kernel<8>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
+  }
+  D3_CUDA_TRY(e, "fetch_gemv13_kernel launch");
+  return (stages & 2) ? run_gemv2(gp, st, pdl) : D3_OK;
 }
 
 int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,

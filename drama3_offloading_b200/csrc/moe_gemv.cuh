@@ -62,6 +62,21 @@ struct GemvParams {
   const __nv_bfloat16* sgate;  // [H]
   float* hs;                   // [T, I] workspace
   float* gs;                   // [T] workspace: sigmoid(x . sgate)
+  // gemv2 loads its first W2 rows before griddepcontrol.wait (1), or only
+  // after it (0: the preceding launch may still be writing W2, as the fetch +
+  // gate/up overlap launch does)
+  int w2_early;
+};
+
+// Fetch + gate/up overlap: which queued fetch job (if any) fills each pair's
+// slot, and how the gate/up units learn that a job's W13/S13 bytes landed.
+struct GemvOverlap {
+  const int* s_job;                  // [pairs] in shared memory: job or -1 (resident)
+  const unsigned long long* done;    // [jobs] W13+S13 vectors landed
+  unsigned long long need;           // vectors per job in those buffers
+  int* err;
+  int err_code;
+  unsigned long long budget_ns;
 };
 
 __device__ __forceinline__ int gemv_pair_id(const void* ids, int bytes, int i, int n) {
@@ -117,96 +132,127 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// CPL = 16-byte chunks per lane of a W13 row = H / 512.
+// The gate/up units of warp gw of nw: routed (pair, row) units, then the
+// shared expert's (token, row) units, then one gate unit per token.  With an
+// overlap context, pass 0 runs the units whose expert is resident (and the
+// shared expert's) and pass 1 the units of fetched experts, each after a
+// bounded wait until its job's W13/S13 bytes have landed.
 template <int CPL>
-__global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) {
-  pdl_wait();
-  pdl_trigger();
+__device__ __forceinline__ void gemv13_units(const GemvParams& p, long gw, long nw,
+                                             const GemvOverlap* ov) {
   const int lane = threadIdx.x & 31;
-  const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const long nw = ((long)gridDim.x * blockDim.x) >> 5;
   const int I = p.I, H = p.H, nkb = H / 128;
   const long routed = (long)p.T * p.topk * I;
-  // after the routed (pair, row) units: the shared expert's (token, row)
-  // units, then one gate unit per token
   const long units = routed + (p.sw13 ? (long)p.T * I + (p.sgate ? p.T : 0) : 0);
   float xv[CPL][16];
   int cur_t = -1;
-  for (long u = gw; u < units; u += nw) {
-    if (u >= routed) {  // shared expert (warp-uniform branch)
-      const long v = u - routed;
-      const bool gate_unit = v >= (long)p.T * I;
-      const int t = gate_unit ? (int)(v - (long)p.T * I) : (int)(v / I);
-      const int j = gate_unit ? 0 : (int)(v - (long)t * I);
+  unsigned long long ready = 0;  // jobs this warp has seen complete
+  const int npass = ov ? 2 : 1;
+  for (int pass = 0; pass < npass; ++pass) {
+    for (long u = gw; u < units; u += nw) {
+      if (u >= routed) {  // shared expert (warp-uniform branch)
+        if (pass == 1) continue;
+        const long v = u - routed;
+        const bool gate_unit = v >= (long)p.T * I;
+        const int t = gate_unit ? (int)(v - (long)p.T * I) : (int)(v / I);
+        const int j = gate_unit ? 0 : (int)(v - (long)t * I);
+        if (t != cur_t) {
+          cur_t = t;
+          const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * H);
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) {
+            const int q = lane + 32 * c;
+            unpack_bf16x8(xr[2 * q], xv[c]);
+            unpack_bf16x8(xr[2 * q + 1], xv[c] + 8);
+          }
+        }
+        const uint4* rg = reinterpret_cast<const uint4*>(gate_unit ? p.sgate
+                                                                   : p.sw13 + (size_t)j * H);
+        float ag = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int q = lane + 32 * c;
+          ag += dot16_bf16(__ldcg(rg + 2 * q), __ldcg(rg + 2 * q + 1), xv[c]);
+        }
+        ag = warp_sum(ag);
+        if (gate_unit) {
+          if (lane == 0) p.gs[t] = 1.f / (1.f + expf(-ag));
+          continue;
+        }
+        const uint4* ru = reinterpret_cast<const uint4*>(p.sw13 + (size_t)(I + j) * H);
+        float au = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int q = lane + 32 * c;
+          au += dot16_bf16(__ldcg(ru + 2 * q), __ldcg(ru + 2 * q + 1), xv[c]);
+        }
+        au = warp_sum(au);
+        if (lane == 0) p.hs[(size_t)t * I + j] = ag / (1.f + expf(-ag)) * au;
+        continue;
+      }
+      const int pair = (int)(u / I), j = (int)(u - (long)pair * I);
+      const int e = gemv_pair_id(p.ids, p.ids_bytes, pair, p.n);
+      if (e < 0) continue;  // warp-uniform: the whole warp works on one unit
+      if (ov) {
+        const int job = ov->s_job[pair];
+        if ((job >= 0) != (pass == 1)) continue;
+        if (job >= 0 && !((ready >> job) & 1ull)) {
+          bool ok = true;
+          if (lane == 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while (ld_acquire_gpu_u64(ov->done + job) < ov->need) {
+              if (globaltimer_ns() - t0 > ov->budget_ns) { ok = false; break; }
+              __nanosleep(128);
+            }
+            if (!ok) atomicCAS(ov->err, 0, ov->err_code);
+          }
+          __syncwarp();  // the other lanes read the slot after lane 0's acquire
+          ready |= 1ull << job;
+        }
+      }
+      const uint4* wg = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + j) * H);
+      const uint4* wu = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + I + j) * H);
+      uint4 g[CPL], v[CPL];
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        g[c] = __ldcg(wg + lane + 32 * c);
+        v[c] = __ldcg(wu + lane + 32 * c);
+      }
+      const int t = pair / p.topk;
       if (t != cur_t) {
         cur_t = t;
         const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * H);
 #pragma unroll
         for (int c = 0; c < CPL; ++c) {
-          const int q = lane + 32 * c;
+          const int q = lane + 32 * c;  // K elements [16q, 16q + 16)
           unpack_bf16x8(xr[2 * q], xv[c]);
           unpack_bf16x8(xr[2 * q + 1], xv[c] + 8);
         }
       }
-      const uint4* rg = reinterpret_cast<const uint4*>(gate_unit ? p.sgate
-                                                                 : p.sw13 + (size_t)j * H);
-      float ag = 0.f;
+      const float* sg = p.s13 + ((size_t)e * (2 * I / 128) + j / 128) * nkb;
+      const float* su = p.s13 + ((size_t)e * (2 * I / 128) + (I + j) / 128) * nkb;
+      float ag = 0.f, au = 0.f;
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
-        const int q = lane + 32 * c;
-        ag += dot16_bf16(__ldcg(rg + 2 * q), __ldcg(rg + 2 * q + 1), xv[c]);
+        const int kb = (lane + 32 * c) >> 3;
+        ag = fmaf(__ldcg(sg + kb), dot16_e4m3(g[c], xv[c]), ag);
+        au = fmaf(__ldcg(su + kb), dot16_e4m3(v[c], xv[c]), au);
       }
       ag = warp_sum(ag);
-      if (gate_unit) {
-        if (lane == 0) p.gs[t] = 1.f / (1.f + expf(-ag));
-        continue;
-      }
-      const uint4* ru = reinterpret_cast<const uint4*>(p.sw13 + (size_t)(I + j) * H);
-      float au = 0.f;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int q = lane + 32 * c;
-        au += dot16_bf16(__ldcg(ru + 2 * q), __ldcg(ru + 2 * q + 1), xv[c]);
-      }
       au = warp_sum(au);
-      if (lane == 0) p.hs[(size_t)t * I + j] = ag / (1.f + expf(-ag)) * au;
-      continue;
+      if (lane == 0) p.h[u] = ag / (1.f + expf(-ag)) * au;
     }
-    const int pair = (int)(u / I), j = (int)(u - (long)pair * I);
-    const int e = gemv_pair_id(p.ids, p.ids_bytes, pair, p.n);
-    if (e < 0) continue;  // warp-uniform: the whole warp works on one unit
-    const uint4* wg = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + j) * H);
-    const uint4* wu = reinterpret_cast<const uint4*>(p.w13 + ((size_t)e * 2 * I + I + j) * H);
-    uint4 g[CPL], v[CPL];
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-      g[c] = __ldcg(wg + lane + 32 * c);
-      v[c] = __ldcg(wu + lane + 32 * c);
-    }
-    const int t = pair / p.topk;
-    if (t != cur_t) {
-      cur_t = t;
-      const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * H);
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int q = lane + 32 * c;  // K elements [16q, 16q + 16)
-        unpack_bf16x8(xr[2 * q], xv[c]);
-        unpack_bf16x8(xr[2 * q + 1], xv[c] + 8);
-      }
-    }
-    const float* sg = p.s13 + ((size_t)e * (2 * I / 128) + j / 128) * nkb;
-    const float* su = p.s13 + ((size_t)e * (2 * I / 128) + (I + j) / 128) * nkb;
-    float ag = 0.f, au = 0.f;
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-      const int kb = (lane + 32 * c) >> 3;
-      ag = fmaf(__ldcg(sg + kb), dot16_e4m3(g[c], xv[c]), ag);
-      au = fmaf(__ldcg(su + kb), dot16_e4m3(v[c], xv[c]), au);
-    }
-    ag = warp_sum(ag);
-    au = warp_sum(au);
-    if (lane == 0) p.h[u] = ag / (1.f + expf(-ag)) * au;
   }
+}
+
+// CPL = 16-byte chunks per lane of a W13 row = H / 512.
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+  gemv13_units<CPL>(p, gw, nw, nullptr);
 }
 
 // CPL = 16-byte chunks per lane of a W2 row = I / 512.  Grid (H / 8 / rpw, T);
@@ -232,7 +278,7 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
 #pragma unroll
   for (int q = 0; q < kGemvPairGroup; ++q) {
     const int e = __shfl_sync(0xffffffffu, my_e, q);
-    if (q < topk && e >= 0 && j_first < H) {
+    if (p.w2_early && q < topk && e >= 0 && j_first < H) {
       const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
@@ -273,7 +319,7 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
     float acc = 0.f;
     for (int k0 = 0; k0 < topk; k0 += kGemvPairGroup) {
       uint4 w[kGemvPairGroup][CPL];
-      if (r == 0 && k0 == 0) {
+      if (r == 0 && k0 == 0 && p.w2_early) {
 #pragma unroll
         for (int q = 0; q < kGemvPairGroup; ++q)
 #pragma unroll

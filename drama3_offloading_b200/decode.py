@@ -11,10 +11,14 @@ Per layer and decode token (batch 1):
    of Drama-3 (notes/01-static-findings.md:54-55, :80-82).  Plain cuBLAS
    GEMVs: not part of the hot path.
 2. router ``d3_router_topk`` on the layer's bf16 gate [256, 2048].
-3. ``d3_resolve_fetch``: device slot allocator + fetch of the missed experts
-   from pinned host memory into the layer's device cache.
-4. ``d3_moe_fp8_forward_shared`` on the cache slots plus the layer's gated
-   bf16 shared expert (resident, 6 MiB), accumulated into ``h``.
+3. ``d3_resolve_fetch_moe`` (default, ``overlap=True``): device slot
+   allocator; ONE launch that fetches the missed experts from pinned host
+   memory into the layer's device cache on 64 CTAs while the other CTAs run
+   the gate/up products of the resident experts and of the layer's gated bf16
+   shared expert (resident, 6 MiB), then those of each fetched expert once its
+   bytes have landed; then the down projection, accumulated into ``h``.
+   (``overlap=False``: ``d3_resolve_fetch``, then ``d3_moe_fp8_forward_shared``
+   on the cache slots.)
 
 Routing: the router runs every layer (its cost is real), but the expert ids
 fed to the cache come from the seeded Zipf(1.1) trace so hit rates are those
@@ -40,8 +44,9 @@ class DecodeStack:
                  topk: int = 8, cache_gib: float = 8.0, capacity: int | None = None,
                  dense_gib: float = DENSE_GIB, trace: np.ndarray | None = None, device="cuda",
                  policy: str = "lru", seed: int = 0, fill: str = "random", group=None,
-                 local_rank: int = 0, trace_offset: int = 0):
+                 local_rank: int = 0, trace_offset: int = 0, overlap: bool = True):
         self.device = dev = torch.device(device)
+        self.overlap = overlap
         self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
         per_expert = 2 * inter * hidden + hidden * inter + 4 * (2 * inter * hidden + hidden * inter) // (128 * 128)
         self.capacity = capacity or max(1, int(cache_gib * (1 << 30)) // (layers * per_expert))
@@ -96,6 +101,20 @@ class DecodeStack:
         if events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
+        if self.overlap:
+            # allocator, then fetch + gate/up in one launch, then the down
+            # projection (the timing sample splits the call after the fetch)
+            run = lambda stages: devcache.dev_resolve_fetch_moe(
+                ex, cur_ids[l], h, self.wts, out=h, accumulate=True, shared=self.shared[l],
+                stages=stages)
+            if events is None:
+                run(3)
+                return
+            run(1)
+            e1.record()
+            events.append((e0, e1))
+            run(2)
+            return
         slots = devcache.dev_resolve_and_fetch(ex, cur_ids[l])
         if events is not None:
             e1.record()
@@ -133,8 +152,9 @@ class DecodeStack:
 
     def sample_fetch_timing(self, steps: int) -> dict:
         """Eager decode steps with CUDA events around every layer's allocator +
-        fetch launch pair (same stream): bytes fetched and device time, for the
-        fetch kernel's achieved host-link bandwidth."""
+        fetch launch pair (with overlap: allocator + fetch/gate-up launches;
+        same stream): bytes fetched and device time, for the fetch kernel's
+        achieved host-link bandwidth."""
         evs = []
         c0 = self.store.counters()
         for _ in range(steps):
@@ -150,8 +170,9 @@ class DecodeStack:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched per token: router, allocator, fetch,
-        and the batch-1 expert path's gate/up and down launches per layer."""
-        return 5 * self.L
+        and the batch-1 expert path's gate/up and down launches per layer
+        (with overlap the fetch and the gate/up products are one launch)."""
+        return (4 if self.overlap else 5) * self.L
 
     def roofline_ms(self, hits: float, misses: float, hbm_gbs: float, host_gbs: float) -> float:
         """t >= dense/HBM + hits*expert/HBM + misses*expert/host per token."""

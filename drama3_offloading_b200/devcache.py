@@ -21,6 +21,14 @@ fallback.  ``FETCH_BACKEND``:
   buffer, ``CPP_BLOCKS_PER_JOB`` CTAs per job) on this library's kernels
   (``d3_resolve_slots`` + ``d3_fetch_experts``), kept for A/B comparison.
 
+Decode steps (one routed row) of ``dev_cached_forward`` go through
+``dev_resolve_fetch_moe`` when ``OVERLAP`` is on (default, ``"b200"`` only):
+the allocator launch, then ONE launch that fetches the misses on a few CTAs
+while the others run the gate/up products of the resident experts (and of the
+shared expert) and then of each fetched expert as soon as its bytes have
+landed, then the down projection (``d3_resolve_fetch_moe``).  Same slots,
+same bits as resolve + fetch followed by ``moe.fp8_moe_forward``.
+
 ``"triton"`` is rejected with ValueError.  Every call is sync-free and keeps a
 static launch shape, so it can be captured into a CUDA graph and replayed with
 new ids (the slot table, step counter and job count live on the device).
@@ -41,6 +49,8 @@ EXPERT_BYTES = 3_146_496
 FETCH_BACKEND = "b200"
 CPP_BLOCKS_PER_JOB = 64
 FETCH_CTAS = 0          # fused fetch grid; 0 = one CTA per SM
+OVERLAP = True          # decode: fetch + gate/up in one launch (d3_resolve_fetch_moe)
+OVERLAP_FETCH_CTAS = 64  # CTAs that fetch inside that launch; the rest run the gate/up units
 POLICY = "lru"
 K_MAX = 64              # largest k one resolve call accepts
 
@@ -183,6 +193,57 @@ def dev_resolve_and_fetch(experts, topk_ids: torch.Tensor, stream=None) -> torch
     return experts._dc_out[:k]
 
 
+def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
+                          topk_weights: torch.Tensor, out: torch.Tensor | None = None,
+                          accumulate: bool = False, shared: tuple | None = None,
+                          stream=None, stages: int = 3) -> torch.Tensor:
+    """One decode row through the cache: resolve ``topk_ids`` [1, k], fetch the
+    misses while the gate/up products of the resident experts run, then the
+    down projection into ``out`` (bf16 [1, H]; added to it with
+    ``accumulate``).  ``shared=(w13_s, w2_s, gate_s)`` adds the shared expert
+    inside the same launches.  Sync-free and graph-capturable.  ``stages``
+    1 / 2 run only the allocator + fetch/gate-up launches / only the down
+    projection (to time them apart); 3 runs all."""
+    from . import moe
+    ids = _ids_arg(topk_ids)
+    k = ids.numel()
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[0] != 1 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous bf16 [1, H] row")
+    H = x.shape[1]
+    I = experts._dc_w2.shape[2]
+    w = topk_weights.reshape(k)
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.to(torch.float32)
+    w = w.contiguous()
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs an out tensor")
+        out = torch.empty(1, H, dtype=torch.bfloat16, device=x.device)
+    sw13 = sw2 = sg = None
+    if shared is not None:
+        sw13, sw2, sg = shared
+    need = int(_lib.load().d3_resolve_fetch_moe_workspace_size(k, H, I))
+    if need == 0:
+        raise ValueError(f"unsupported shape k={k} H={H} I={I}")
+    ws = moe._workspace(x.device, need, "overlap")
+    _lib.call("d3_resolve_fetch_moe", ctypes.byref(experts._dc_desc), _lib.ptr(ids),
+              ids.element_size(), k, _lib.ptr(x), _lib.ptr(w),
+              1 if w.dtype == torch.float32 else 0, H, I,
+              _lib.ptr(sw13) if sw13 is not None else None,
+              _lib.ptr(sw2) if sw2 is not None else None,
+              _lib.ptr(sg) if sg is not None else None, _lib.ptr(out), 1 if accumulate else 0,
+              _lib.ptr(moe.error_word(x.device)), _lib.ptr(ws), ws.numel(),
+              int(OVERLAP_FETCH_CTAS), int(stages), _lib.stream_ptr(stream))
+    return out
+
+
+def _overlap_ok(experts, topk_ids, x) -> bool:
+    H = x.shape[-1]
+    I = experts._dc_w2.shape[2]
+    return (OVERLAP and FETCH_BACKEND == "b200" and x.dim() == 2 and x.shape[0] == 1
+            and H % 512 == 0 and I % 512 == 0 and experts._dc_cap >= topk_ids.numel())
+
+
 def dev_cached_forward(self, x, topk_ids, topk_weights):
     """``MoEExperts.forward`` through the device cache (bin/devcache.py:258-277).
 
@@ -194,6 +255,8 @@ def dev_cached_forward(self, x, topk_ids, topk_weights):
     if topk_ids.shape[0] != 1 or not getattr(self, "_dc_cap", 0):
         from . import offload
         return offload.offloaded_forward(self, x, topk_ids, topk_weights)
+    if _overlap_ok(self, topk_ids, x):
+        return dev_resolve_fetch_moe(self, topk_ids, x.contiguous(), topk_weights)
     slots = dev_resolve_and_fetch(self, topk_ids)
     return moe.fp8_moe_forward(x, slots.reshape(topk_ids.shape), topk_weights, self._dc_w13,
                                self._dc_s13, self._dc_w2, self._dc_s2)

@@ -126,6 +126,33 @@ typedef struct d3_layer_cache {
 D3_API int d3_resolve_fetch(const d3_layer_cache* layer, const void* ids, int32_t ids_bytes,
                      int32_t k, int32_t fetch_ctas, d3_stream_t stream);
 
+/* One decode row (T = 1, k ids) through the layer's cache with the fetch and
+ * the expert compute overlapped: the allocator launch (as d3_resolve_fetch),
+ * then ONE launch in which fetch_ctas CTAs (0 = 64) move the misses -- the
+ * W13/S13 bytes of every job first -- while the other CTAs run the gate/up
+ * products of the resident experts and of the optional shared expert, then
+ * those of each fetched expert after a bounded wait (2 s; *err_word = 41 on
+ * expiry) until its job's W13/S13 bytes have landed; then the down projection
+ * into out (bf16 [1, H], added when accumulate).  layer: the 4 buffers w13
+ * [C][2I][H] e4m3, w2 [C][H][I], s13 [C][2I/128][H/128] f32, s2
+ * [C][H/128][I/128] f32, capacity >= k; H, I as for the decode path of
+ * d3_moe_fp8_forward_shared (multiples of 512).  workspace: at least
+ * d3_resolve_fetch_moe_workspace_size(k, H, I) bytes, 16-byte aligned.  Same
+ * slot tables and the same output bits as d3_resolve_fetch followed by
+ * d3_moe_fp8_forward(_shared) over the cache.  Replaces the reference's decode
+ * step of dev_cached_forward (bin/devcache.py:258-277: dev_resolve_and_fetch,
+ * then fp8_moe_forward over the cache).  stages: 3 = all of it; 1 = the
+ * allocator and the fetch/gate-up launch only, 2 = the down projection only
+ * (same arguments and workspace; for timing the two halves apart). */
+D3_API size_t d3_resolve_fetch_moe_workspace_size(int32_t k, int32_t H, int32_t I);
+D3_API int d3_resolve_fetch_moe(const d3_layer_cache* layer, const void* ids, int32_t ids_bytes,
+                                int32_t k, const void* x, const void* weights,
+                                int32_t weights_f32, int32_t H, int32_t I,
+                                const void* shared_w13, const void* shared_w2,
+                                const void* shared_gate, void* out, int32_t accumulate,
+                                int32_t* err_word, void* workspace, size_t workspace_bytes,
+                                int32_t fetch_ctas, int32_t stages, d3_stream_t stream);
+
 /* Only the fetch half of d3_resolve_fetch: copy the jobs already queued in
  * layer->fetch_slot / fetch_expert / *nmiss (e.g. by d3_resolve_slots or a
  * host-written job list) for all nbuf buffers, one launch of fetch_ctas CTAs

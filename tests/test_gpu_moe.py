@@ -228,6 +228,44 @@ def test_dev_cached_forward_equals_resident(cap):
     moe.check_errors(DEV)
 
 
+@pytest.mark.parametrize("cap,shared,acc,fetch_ctas", [(12, True, True, 32), (8, False, False, 32),
+                                                      (24, True, False, 5), (64, True, True, 148)])
+def test_fetch_gate_up_overlap_matches_separate_launches(cap, shared, acc, fetch_ctas):
+    """d3_resolve_fetch_moe (fetch + gate/up in one launch, each fetched
+    expert's gate/up after its bytes land) against d3_resolve_fetch followed
+    by the decode MoE call over the cache: the same slot tables and
+    bit-identical outputs, step after step (misses, hits, evictions)."""
+    E, H, I = 64, 2048, 512
+    ref = synth.make_experts(E, seed=9, device="cuda", style="test")
+    a, b = ref.to("cpu").pin(), ref.to("cpu").pin()
+    devcache.init_dev_cache(a, DEV, cap)
+    devcache.init_dev_cache(b, DEV, cap)
+    sh = tuple(t.to(DEV) if t is not None else None for t in _shared(H, I, seed=cap)) \
+        if shared else None
+    g = torch.Generator().manual_seed(100 + cap)
+    old = devcache.OVERLAP_FETCH_CTAS
+    devcache.OVERLAP_FETCH_CTAS = fetch_ctas
+    try:
+        for step in range(30):
+            x = torch.randn(1, H, generator=g).to(torch.bfloat16).to(DEV)
+            ids = torch.randperm(E if step % 3 else 16, generator=g)[:8].unsqueeze(0).to(DEV)
+            w = torch.rand(1, 8, generator=g).to(DEV)
+            base = torch.randn(1, H, generator=g).to(torch.bfloat16).to(DEV)
+            out_a, out_b = base.clone(), base.clone()
+            devcache.dev_resolve_fetch_moe(a, ids, x, w, out=out_a, accumulate=acc, shared=sh)
+            slots = devcache.dev_resolve_and_fetch(b, ids)
+            moe.fp8_moe_forward(x, slots.reshape(1, 8), w, b._dc_w13, b._dc_s13, b._dc_w2,
+                                b._dc_s2, out=out_b, accumulate=acc, shared=sh)
+            torch.cuda.synchronize()
+            assert torch.equal(a._dc_out, b._dc_out), f"step {step}"
+            assert torch.equal(a._dc_slot_expert, b._dc_slot_expert), f"step {step}"
+            assert torch.equal(out_a, out_b), f"step {step}"
+    finally:
+        devcache.OVERLAP_FETCH_CTAS = old
+    moe.check_errors(DEV)
+    assert torch.equal(a._dc_w13, b._dc_w13) and torch.equal(a._dc_s2, b._dc_s2)
+
+
 @pytest.mark.parametrize("T", [1, 5])   # CUDA-core path / tensor-core path
 def test_moe_forward_accumulate_into_input(T):
     """accumulate=True with out aliasing x: h <- h + moe(h) (the residual add)."""
