@@ -90,6 +90,7 @@ constexpr int kMaxExperts = 8192;
 constexpr int kMaxPairs = 65536;
 constexpr int kFusedQuantMaxPairs = 4096;  // route quantises in-launch up to this many pairs
 constexpr int kRouteSmemBudget = 160 * 1024;  // route launch: shared memory for the sort
+constexpr int kRouteKeep = 4;                  // 32-pair batches per warp whose ids stay in registers
 
 struct Plan {
   int P;        // routed pairs = T * topk
@@ -209,7 +210,7 @@ __device__ __forceinline__ int pick_split(int tiles, int nkb, int lo, int hi, in
 // pair at off[e] + base[w][e] + (rank among the equal ids of its 32-pair
 // batch) -- exactly the order of a sequential walk.
 // Dynamic shared memory (ints): cnt[n], off[n], tile prefix[n], hist[NW][n],
-// then sorted[P] when the quantisation is fused.
+// then the pair -> sorted row map [P] when the quantisation is fused.
 __device__ __forceinline__ int route_chunk(int P, int nw) {
   const int batches = (P + 31) / 32;
   return (batches + nw - 1) / nw * 32;
@@ -222,28 +223,52 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   int* s_off = sm + n;            // [n]
   int* s_tp = sm + 2 * n;         // [n] exclusive prefix of N tiles per expert
   int* hist = sm + 3 * n;         // [NW][n]
-  int* s_sorted = hist + (size_t)NW * n;  // [P] (fused quantisation only)
+  int* s_inv = hist + (size_t)NW * n;     // [P] pair -> sorted row (fused quantisation only)
   __shared__ int warp_tot[32], wt2[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool lead = blockIdx.x == 0;
   pdl_trigger();
   pdl_wait();
-  if (p.wait_flags && warp == 0) {
-    // the rows and ids come from the other ranks; the barrier after the
-    // histogram reset orders every thread's reads after this acquire
-    if (!warp_wait_epochs(p.wait_flags, p.wait_n, *p.wait_epoch, p.wait_budget) && lane == 0)
+  if (p.wait_flags) {
+    // the rows and ids come from the other ranks: every thread reads them
+    // only after this acquire (CTA barrier)
+    if (warp == 0 &&
+        !warp_wait_epochs(p.wait_flags, p.wait_n, *p.wait_epoch, p.wait_budget) && lane == 0)
       atomicCAS(p.wait_err, 0, p.wait_code);
+    __syncthreads();
   }
   for (int i = tid; i < NW * n; i += blockDim.x) hist[i] = 0;
+  // this warp's first sweep of quantisation units (pair, K block), over all
+  // pairs: the activation rows are known by pair index, so their loads are
+  // in flight together with the ids'; rows of skipped pairs are never stored
+  const int nkb = p.H / 128;
+  const long long qunits = p.fuse_quant ? (long long)p.P * nkb : 0;
+  const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
+  const int gwarps = gridDim.x * (blockDim.x >> 5);
+  float xv[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const long long u = (long long)gwarp * 4 + q;
+    if (u < qunits) {
+      const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
+      load_x_block(p.x, pair, p.topk, p.H, kb, xv[q]);
+    }
+  }
   __syncthreads();
   const int C = route_chunk(p.P, NW);
-  // ---- pass 1: per-chunk counts (leaders of a batch hold distinct ids)
+  // ---- pass 1: per-chunk counts (leaders of a batch hold distinct ids);
+  // the first kRouteKeep batches' ids stay in registers for pass 2
+  int keep[kRouteKeep];
   if (warp < NW) {
     int* h = hist + (size_t)warp * n;
     const int end = min(p.P, (warp + 1) * C);
-    for (int b0 = warp * C; b0 < end; b0 += 32) {
+    int bi = 0;
+    for (int b0 = warp * C; b0 < end; b0 += 32, ++bi) {
       const int i = b0 + lane;
       const int e = i < end ? load_pair_id(p.ids, p.ids_bytes, i, n) : -1;
+#pragma unroll
+      for (int q = 0; q < kRouteKeep; ++q)
+        if (bi == q) keep[q] = e;
       const unsigned m = __match_any_sync(0xffffffffu, e);
       if (e >= 0 && lane == __ffs(m) - 1) h[e] += __popc(m);
       __syncwarp();
@@ -306,9 +331,17 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   if (warp < NW) {
     int* h = hist + (size_t)warp * n;
     const int end = min(p.P, (warp + 1) * C);
-    for (int b0 = warp * C; b0 < end; b0 += 32) {
+    int bi = 0;
+    for (int b0 = warp * C; b0 < end; b0 += 32, ++bi) {
       const int i = b0 + lane;
-      const int e = i < end ? load_pair_id(p.ids, p.ids_bytes, i, n) : -1;
+      int e = -1;
+      if (bi < kRouteKeep) {
+#pragma unroll
+        for (int q = 0; q < kRouteKeep; ++q)
+          if (bi == q) e = keep[q];
+      } else if (i < end) {
+        e = load_pair_id(p.ids, p.ids_bytes, i, n);
+      }
       const unsigned m = __match_any_sync(0xffffffffu, e);
       const int leader = __ffs(m) - 1;
       int base = 0;
@@ -321,9 +354,9 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
         int pos = -1;
         if (e >= 0) {
           pos = s_off[e] + base + __popc(m & ((1u << lane) - 1));
-          if (p.fuse_quant) s_sorted[pos] = i;
           if (lead) p.sorted[pos] = i;
         }
+        if (p.fuse_quant) s_inv[i] = pos;
         if (lead) p.inv[i] = pos;
       }
       __syncwarp();
@@ -335,30 +368,32 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   __syncthreads();
   const int gthreads = gridDim.x * blockDim.x;
   const int gtid = blockIdx.x * blockDim.x + tid;
-  if (p.fuse_quant) {
-    // only the valid rows: the GEMM never uses a column past an expert's
-    // pair count, so padding rows need no planes; four blocks per warp with
-    // their loads issued together
-    const int nkb = p.H / 128;
-    const int nblk = nvalid * nkb;
-    const int gwarps = gthreads >> 5;
-    for (int w0 = (gtid >> 5) * 4; w0 < nblk; w0 += gwarps * 4) {
-      float xv[4][4];
+  // ---- the quantisation units: hi/lo planes + scale of each valid pair's
+  // row at its sorted position (the GEMM never reads a row past an
+  // expert's pair count, so skipped pairs get none)
+  for (long long u0 = (long long)gwarp * 4; u0 < qunits; u0 += (long long)gwarps * 4) {
+    const bool first = u0 == (long long)gwarp * 4;
+    float v[4][4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int wu = w0 + u;
-        if (wu < nblk) {
-          const int row = wu / nkb, kb = wu - row * nkb;
-          load_x_block(p.x, s_sorted[row], p.topk, p.H, kb, xv[u]);
+    for (int q = 0; q < 4; ++q) {
+      const long long u = u0 + q;
+      if (u < qunits) {
+        const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
+        if (first) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v[q][c] = xv[q][c];
+        } else {
+          load_x_block(p.x, pair, p.topk, p.H, kb, v[q]);
         }
       }
+    }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int wu = w0 + u;
-        if (wu < nblk) {
-          const int row = wu / nkb, kb = wu - row * nkb;
-          store_x_block(xv[u], p.H, row, kb, p.xq, p.xs);
-        }
+    for (int q = 0; q < 4; ++q) {
+      const long long u = u0 + q;
+      if (u < qunits) {
+        const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
+        const int row = s_inv[pair];
+        if (row >= 0) store_x_block(v[q], p.H, row, kb, p.xq, p.xs);
       }
     }
   }
