@@ -3,8 +3,9 @@
 Runs the REFERENCE's own Triton kernels -- ``_resolve_slots`` and
 ``_fetch_experts`` from ``bin/devcache.py`` -- on CPU tensors under
 ``TRITON_INTERPRET=1`` and records their outputs.  This needs the reference
-checkout (``--reference``, default the path it was surveyed at) and only runs
-on the development container; the committed ``.npz`` files travel instead.
+checkout (``--reference``, or the ``D3_REFERENCE_DIR`` environment variable)
+and only runs where that checkout exists; the committed ``.npz`` files travel
+instead.
 
     python tests/golden/make_golden.py --reference <path-to-drama3-offloading>
 
@@ -39,9 +40,11 @@ sys.path.insert(0, str(HERE.parent.parent))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("D3_REFERENCE_DIR"))
     ap.add_argument("--out", default=str(HERE / "resolve_golden.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path-to-drama3-offloading> (or set D3_REFERENCE_DIR)")
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, str(Path(args.reference) / "bin"))
     import torch
