@@ -74,6 +74,49 @@ def test_argument_validation_without_gpu():
     assert lib.d3_trace_append(z, 4, 1, 8, 0, P(0), z, 4, P(0)) == -1
 
 
+def test_folded_entry_points_validate_without_gpu():
+    """The overlapped decode call and the folded NVLink expert-parallel calls
+    reject bad shapes and descriptors before touching the GPU."""
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    z = P(16)
+    I64 = ctypes.c_int64
+    # d3_resolve_fetch_moe: workspace size, shape, buffer layout, capacity < k
+    assert lib.d3_resolve_fetch_moe_workspace_size(8, 2048, 512) >= 512 + 4 * (8 * 512 + 513)
+    assert lib.d3_resolve_fetch_moe_workspace_size(0, 2048, 512) == 0
+    d = _lib.LayerCache()
+    d.num_experts, d.capacity, d.policy, d.nbuf = 64, 12, 0, 4
+    sizes = (2 * 512 * 2048, 2048 * 512, 8 * 16 * 4, 16 * 4 * 4)
+    for b, n in enumerate(sizes):
+        d.host[b], d.cache[b], d.bytes[b] = 16, 16, n
+    ws = ctypes.c_size_t(1 << 20)
+    call = lambda desc, k, H, I, wsz: lib.d3_resolve_fetch_moe(
+        ctypes.byref(desc), z, 4, k, z, z, 1, H, I, None, None, None, z, 0, z, z, wsz, 0, 3, P(0))
+    assert call(d, 8, 2048, 384, ws) == -5          # I not a multiple of 512
+    d.bytes[1] = 1234
+    assert call(d, 8, 2048, 512, ws) == -1          # buffer sizes do not match H, I
+    d.bytes[1] = sizes[1]
+    d.capacity = 4
+    assert call(d, 8, 2048, 512, ws) == -5          # capacity < k
+    d.capacity = 12
+    assert call(d, 8, 2048, 512, ctypes.c_size_t(64)) == -7   # workspace too small
+    d.nbuf = 3
+    assert call(d, 8, 2048, 512, ws) == -1          # not the 4-buffer layout
+    # d3_moe_fp8_forward_p2p: T must be n_ranks * cap, ranks in range
+    arr = (P * 2)(16, 16)
+    p2p = lambda T, n_ranks, rank, cap: lib.d3_moe_fp8_forward_p2p(
+        z, z, 4, z, 1, T, 1, z, z, z, z, 32, 2048, 512, z, z, ctypes.c_size_t(1 << 20), z, z,
+        n_ranks, rank, cap, arr, arr, z, 31, I64(10**9), P(0))
+    assert p2p(100, 2, 0, 64) == -1
+    assert p2p(128, 2, 2, 64) == -1
+    assert p2p(128, 17, 0, 64) == -6
+    # d3_ep_combine_p2p: rank count and wait budget
+    comb = lambda n_ranks, budget: lib.d3_ep_combine_p2p(
+        z, z, z, 1, 8, 8, 2048, z, 0, z, n_ranks, z, z, 32, I64(budget), P(0))
+    assert comb(0, 10**9) == -6
+    assert comb(2, 0) == -1
+
+
 def test_layer_cache_struct_layout():
     # 4 int32, 11 pointers, 4+4 pointers, 4 int64
     assert ctypes.sizeof(_lib.LayerCache) == 16 + 11 * 8 + 8 * 8 + 4 * 8
