@@ -817,8 +817,9 @@ def main():
                 "token_roofline_ms": r["roof_ms"],
                 "token_roofline_frac": r["roof_ms"] / (1e3 / tokb),
                 "roofline": {"bound": "host_link",
-                             "kernel": ("fetch_gemv13_kernel (+allocator): the fetch with the "
-                                        "gate/up products overlapped" if not args.no_overlap
+                             "kernel": ("fetch_gemv13_kernel: the fetch with the gate/up "
+                                        "products overlapped (event-timed launch)"
+                                        if not args.no_overlap
                                         else "fetch_layer_kernel (+allocator)"),
                              "achieved": r["fetch_gbs"], "peak": peak, "unit": "GB/s",
                              "frac": r["fetch_gbs"] / peak, "traffic": None,

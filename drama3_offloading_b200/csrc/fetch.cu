@@ -495,7 +495,7 @@ static int launch_fetch(const FetchParams& fp, int fetch_ctas, cudaStream_t st, 
 
 int resolve_for_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
                       int64_t* zero, int32_t nzero, cudaStream_t st, FetchParams* fp,
-                      int64_t* expert_bytes) {
+                      int64_t* expert_bytes, bool launch) {
   D3_CHECK_ARG(L && ids, "d3_resolve_fetch: null pointer");
   D3_CHECK_ARG(ids_bytes == 4 || ids_bytes == 8, "ids_bytes must be 4 or 8");
   D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
@@ -523,7 +523,7 @@ int resolve_for_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_byte
   p.out_slot = L->out_slot; p.fetch_slot = L->fetch_slot; p.fetch_expert = L->fetch_expert;
   p.nmiss = L->nmiss; p.counters = L->counters; p.expert_bytes = *expert_bytes;
   p.zero = zero; p.nzero = nzero;
-  return launch_resolve(p, st);
+  return launch ? launch_resolve(p, st) : D3_OK;
 }
 
 }  // namespace d3

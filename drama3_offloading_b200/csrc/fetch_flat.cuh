@@ -24,9 +24,11 @@ constexpr int kFetchThreads = 256;
 constexpr int kFetchUnroll = 4;
 
 // Resolve launch for one layer (fetch.cu), with `zero` [nzero] int64 cleared
-// by the same launch; fills *fp for a fetch of the queued jobs.
+// by the same launch; fills *fp for a fetch of the queued jobs.  launch =
+// false only validates the descriptor and fills *fp (the jobs queued by an
+// earlier allocator launch).
 int resolve_for_fetch(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
                       int64_t* zero, int32_t nzero, cudaStream_t st, FetchParams* fp,
-                      int64_t* expert_bytes);
+                      int64_t* expert_bytes, bool launch = true);
 
 }  // namespace d3

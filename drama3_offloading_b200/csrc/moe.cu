@@ -165,7 +165,7 @@ struct RouteParams {
   int* wait_err; int wait_code; unsigned long long wait_budget;
   // activation quantisation folded into this launch
   int fuse_quant;
-  const __nv_bfloat16* x; int topk, H, Ppad;
+  const __nv_bfloat16* x; int topk, H;
   uint8_t* xq; float* xs;
 };
 
@@ -850,7 +850,7 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   // kFusedQuantMaxPairs pairs (its CTAs share the rows)
   rp.fuse_quant = P <= kFusedQuantMaxPairs ? 1 : 0;
   rp.x = static_cast<const __nv_bfloat16*>(x);
-  rp.topk = topk; rp.H = H; rp.Ppad = pl.Ppad; rp.xq = xq; rp.xs = xs;
+  rp.topk = topk; rp.H = H; rp.xq = xq; rp.xs = xs;
   if (link) {
     rp.wait_flags = link->wait_flags; rp.wait_epoch = link->epoch; rp.wait_n = link->n_ranks;
     rp.wait_err = link->err; rp.wait_code = link->wait_code; rp.wait_budget = link->budget_ns;
@@ -976,7 +976,7 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
                          int32_t* err_word, void* workspace, size_t workspace_bytes,
                          int32_t fetch_ctas, int32_t stages, d3_stream_t stream) {
   D3_CHECK_ARG(L && ids && x && weights && out && err_word, "d3_resolve_fetch_moe: null pointer");
-  D3_CHECK_ARG(stages >= 1 && stages <= 3, "stages must be 1, 2 or 3");
+  D3_CHECK_ARG(stages >= 1 && stages <= 7, "stages must be a non-empty mask of 1, 2, 4");
   D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
   if (!gemv_shapes_ok(k, H, I))
     return fail(D3_ERR_UNSUPPORTED, "H and I must be 512 x {1,2,4,8} / {1,2,4}");
@@ -1019,12 +1019,15 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   gp.sw2 = static_cast<const __nv_bfloat16*>(shared_w2);
   gp.sgate = static_cast<const __nv_bfloat16*>(shared_gate);
   gp.w2_early = 0;
-  if (!(stages & 1)) return run_gemv2(gp, st, false);  // a call's first launch: no PDL
+  // stages: 1 allocator, 2 fetch + gate/up, 4 down projection; a call's
+  // first launch is an ordinary stream dependent (no programmatic launch)
+  if (!(stages & 3)) return run_gemv2(gp, st, false);
   FetchParams fp{};
   int64_t expert_bytes = 0;
   int rc = resolve_for_fetch(L, ids, ids_bytes, k, reinterpret_cast<int64_t*>(done), 64, st, &fp,
-                             &expert_bytes);
+                             &expert_bytes, (stages & 1) != 0);
   if (rc) return rc;
+  if (!(stages & 2)) return (stages & 4) ? run_gemv2(gp, st, false) : D3_OK;
   FetchOverlapParams o{};
   o.done = done;
   // fetch CTAs, then the rest of one resident wave (2 CTAs per SM) runs the
@@ -1036,7 +1039,7 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   o.err = err_word; o.err_code = 41; o.budget_ns = kOverlapWaitBudgetNs;
   const int grid = 2 * num_sms();
   cudaError_t e;
-  const bool pdl = pdl_enabled();
+  const bool pdl = pdl_enabled() && (stages & 1);
   switch (H / 512) {
     case 1: e = launch_k(fetch_gemv13_kernel<1>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
     case 2: e = launch_k(fetch_gemv13_kernel<2>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
@@ -1044,7 +1047,7 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
     default: e = launch_k(fetch_gemv13_kernel<8>, dim3(grid), dim3(kGemvThreads), 0, st, pdl, fp, gp, o); break;
   }
   D3_CUDA_TRY(e, "fetch_gemv13_kernel launch");
-  return (stages & 2) ? run_gemv2(gp, st, pdl) : D3_OK;
+  return (stages & 4) ? run_gemv2(gp, st, pdl_enabled()) : D3_OK;
 }
 
 int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,

@@ -100,21 +100,24 @@ class DecodeStack:
         ex = self.store.layers[l]
         if events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
         if self.overlap:
             # allocator, then fetch + gate/up in one launch, then the down
-            # projection (the timing sample splits the call after the fetch)
+            # projection (the timing sample brackets the fetch launch alone)
             run = lambda stages: devcache.dev_resolve_fetch_moe(
                 ex, cur_ids[l], h, self.wts, out=h, accumulate=True, shared=self.shared[l],
                 stages=stages)
             if events is None:
-                run(3)
+                run(7)
                 return
             run(1)
+            e0.record()
+            run(2)
             e1.record()
             events.append((e0, e1))
-            run(2)
+            run(4)
             return
+        if events is not None:
+            e0.record()
         slots = devcache.dev_resolve_and_fetch(ex, cur_ids[l])
         if events is not None:
             e1.record()
@@ -151,10 +154,10 @@ class DecodeStack:
         torch.cuda.synchronize(self.device)
 
     def sample_fetch_timing(self, steps: int) -> dict:
-        """Eager decode steps with CUDA events around every layer's allocator +
-        fetch launch pair (with overlap: allocator + fetch/gate-up launches;
-        same stream): bytes fetched and device time, for the fetch kernel's
-        achieved host-link bandwidth."""
+        """Eager decode steps with CUDA events around every layer's fetch
+        (with overlap: the fetch + gate/up launch alone; without: the
+        allocator + fetch launch pair): bytes fetched and device time, for the
+        fetch kernel's achieved host-link bandwidth."""
         evs = []
         c0 = self.store.counters()
         for _ in range(steps):

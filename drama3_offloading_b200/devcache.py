@@ -196,14 +196,14 @@ def dev_resolve_and_fetch(experts, topk_ids: torch.Tensor, stream=None) -> torch
 def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
                           topk_weights: torch.Tensor, out: torch.Tensor | None = None,
                           accumulate: bool = False, shared: tuple | None = None,
-                          stream=None, stages: int = 3) -> torch.Tensor:
+                          stream=None, stages: int = 7) -> torch.Tensor:
     """One decode row through the cache: resolve ``topk_ids`` [1, k], fetch the
     misses while the gate/up products of the resident experts run, then the
     down projection into ``out`` (bf16 [1, H]; added to it with
     ``accumulate``).  ``shared=(w13_s, w2_s, gate_s)`` adds the shared expert
     inside the same launches.  Sync-free and graph-capturable.  ``stages``
-    1 / 2 run only the allocator + fetch/gate-up launches / only the down
-    projection (to time them apart); 3 runs all."""
+    masks the launches issued (1 allocator, 2 fetch + gate/up, 4 down
+    projection; 7 = all), to time them apart."""
     from . import moe
     ids = _ids_arg(topk_ids)
     k = ids.numel()

@@ -141,9 +141,10 @@ D3_API int d3_resolve_fetch(const d3_layer_cache* layer, const void* ids, int32_
  * slot tables and the same output bits as d3_resolve_fetch followed by
  * d3_moe_fp8_forward(_shared) over the cache.  Replaces the reference's decode
  * step of dev_cached_forward (bin/devcache.py:258-277: dev_resolve_and_fetch,
- * then fp8_moe_forward over the cache).  stages: 3 = all of it; 1 = the
- * allocator and the fetch/gate-up launch only, 2 = the down projection only
- * (same arguments and workspace; for timing the two halves apart). */
+ * then fp8_moe_forward over the cache).  stages: a mask of the launches to
+ * issue -- 1 allocator, 2 fetch + gate/up, 4 down projection; 7 = all of it
+ * (same arguments and workspace for the split calls, in that order; for
+ * timing the launches apart). */
 D3_API size_t d3_resolve_fetch_moe_workspace_size(int32_t k, int32_t H, int32_t I);
 D3_API int d3_resolve_fetch_moe(const d3_layer_cache* layer, const void* ids, int32_t ids_bytes,
                                 int32_t k, const void* x, const void* weights,
