@@ -42,14 +42,32 @@ def error_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+# device error codes: which bounded wait gave up
+ERROR_CODES = {
+    1: "expert GEMM: the TMA producer waited for a free pipeline stage",
+    2: "expert GEMM: the MMA issuer waited for loaded operands or a free accumulator",
+    3: "expert GEMM: the final wait for the CTA's own MMAs",
+    4: "expert GEMM: the epilogue waited for an accumulator",
+    31: "expert parallel: a source rank's dispatch never arrived",
+    32: "expert parallel: a serving rank's returned rows never arrived",
+    41: "decode overlap: a fetched expert's bytes never landed",
+}
+
+
+def error_message(code: int) -> str:
+    return ERROR_CODES.get(code, "unknown bounded wait")
+
+
 def check_errors(device=None) -> None:
-    """Raise if any GEMM on ``device`` gave up on a bounded wait."""
+    """Raise if a kernel on ``device`` gave up on a bounded wait (the error
+    word keeps the first code; see ERROR_CODES)."""
     device = torch.device(device or torch.cuda.current_device())
     if device.type != "cuda":
         device = torch.device("cuda", torch.cuda.current_device())
     v = int(error_word(device).item())
     if v:
-        raise RuntimeError(f"d3 MoE GEMM reported device error code {v} (a bounded wait expired)")
+        raise RuntimeError(f"d3 device error code {v}: {error_message(v)} (a bounded wait "
+                           "expired)")
 
 
 def router_topk(x: torch.Tensor, gate_w: torch.Tensor, k: int = 8, renorm: bool = True,

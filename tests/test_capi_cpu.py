@@ -120,3 +120,15 @@ def test_folded_entry_points_validate_without_gpu():
 def test_layer_cache_struct_layout():
     # 4 int32, 11 pointers, 4+4 pointers, 4 int64
     assert ctypes.sizeof(_lib.LayerCache) == 16 + 11 * 8 + 8 * 8 + 4 * 8
+
+
+def test_device_error_codes_are_named():
+    """Every code a kernel writes into the device error word has a message."""
+    from drama3_offloading_b200 import moe
+    src = (Path(__file__).resolve().parent.parent / "drama3_offloading_b200" / "csrc")
+    text = "".join(f.read_text() for f in sorted(src.glob("*.cu*")))
+    codes = {int(c) for c in re.findall(r"gemm_error\(p\.err, (\d+)\)", text)}
+    codes |= {int(c) for c in re.findall(r"err_code = (\d+)", text)}
+    codes |= {31, 32}   # the expert-parallel waits' codes, passed in by ep.py
+    assert codes and codes <= set(moe.ERROR_CODES), codes - set(moe.ERROR_CODES)
+    assert moe.error_message(999) == "unknown bounded wait"
