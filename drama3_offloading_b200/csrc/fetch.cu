@@ -448,8 +448,10 @@ static int launch_resolve(const ResolveParams& p, cudaStream_t st) {
                                      (int)smem),
                 "resolve smem attribute");
   }
-  resolve_kernel<<<1, 32, smem, st>>>(p);
-  return launch_status("resolve_kernel launch");
+  // programmatic launch: resolve reads nothing before griddepcontrol.wait
+  D3_CUDA_TRY(launch_k(resolve_kernel, dim3(1), dim3(32), smem, st, pdl_enabled(), p),
+              "resolve_kernel launch");
+  return D3_OK;
 }
 
 static int make_fetch_params(const d3_layer_cache* L, FetchParams* fp, int64_t* expert_bytes) {

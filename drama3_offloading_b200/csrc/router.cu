@@ -191,6 +191,10 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
   float* s_logits = reinterpret_cast<float*>(smem_raw);  // [T][E], used in the leader
   double* xd = reinterpret_cast<double*>(smem_raw + router_cluster_logit_bytes(p.E));
   cluster_arrive_relaxed();  // "this CTA has started" (phase 1)
+  // programmatic launch: the next launch may start its prologue now; nothing
+  // of global memory is read before the preceding grid has completed
+  pdl_trigger();
+  pdl_wait();
   const unsigned rank = cluster_ctarank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = p.T;        // <= kRouterClusterMaxT
@@ -289,6 +293,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * kRouterTokensPerCta;
   const int nt = min(kRouterTokensPerCta, p.T - t0);
+  pdl_trigger();
+  pdl_wait();
   // stage the token tile (16-byte vectors; H % 8 == 0 is checked on the host)
   const int vec_per_row = p.H / 8;
   for (int i = threadIdx.x; i < nt * vec_per_row; i += blockDim.x) {
@@ -402,13 +408,15 @@ static int launch_router(const RouterParams& p, cudaStream_t st, const char* wha
     cfg.blockDim = dim3(kRouterClusterThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kRouterClusterCtas;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     D3_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, p), what);
     return D3_OK;
   }
@@ -424,8 +432,8 @@ static int launch_router(const RouterParams& p, cudaStream_t st, const char* wha
   if (smem > 48 * 1024)
     D3_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "router smem attribute");
-  k<<<grid, 256, smem, st>>>(p);
-  return launch_status(what);
+  D3_CUDA_TRY(launch_k(k, grid, dim3(256), smem, st, pdl_enabled(), p), what);
+  return D3_OK;
 }
 
 }  // namespace d3
