@@ -215,6 +215,34 @@ def test_p2p_fused_layer_matches_unfused(n_ranks, T):
         assert float(rel) < 1e-2
 
 
+def test_p2p_expert_call_wait_gives_up_and_reports():
+    """The expert call's folded wait on a dispatch flag nothing sets: its route
+    launch gives up after the budget with code 31 in the error word, the call
+    completes (publishing its return epoch) and the stream stays usable."""
+    n_ranks, cap, H = 2, 8, 2048
+    bufs = [_p2p_buffers(n_ranks, cap, H) for _ in range(n_ranks)]
+    b = bufs[0]
+    b["epoch"].fill_(1)              # flag_d stays 0: no source ever dispatched
+    b["recv_eid"].fill_(-1)
+    b["recv_eid"][:3] = torch.tensor([0, 1, 2], dtype=torch.int32, device=DEV)
+    ex = synth.make_experts(4, 2048, 512, seed=1, device=DEV)
+    arr = lambda name: (ctypes.c_void_p * n_ranks)(*(_lib.ptr(x[name]).value for x in bufs))
+    err = moe.error_word(DEV)
+    err.zero_()
+    ones = torch.ones(n_ranks * cap, 1, device=DEV)
+    moe.fp8_moe_forward_p2p(b["recv_x"], b["recv_eid"].view(-1, 1), ones, ex.w13_weight,
+                            ex.w13_scale_inv, ex.w2_weight, ex.w2_scale_inv,
+                            wait_flags=b["flag_d"], epoch=b["epoch"], n_ranks=n_ranks, rank=0,
+                            cap=cap, peer_ret=arr("ret"), peer_flag_r=arr("flag_r"),
+                            counter=b["ctr"][1:], wait_code=31, budget_ns=20_000_000)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 31
+    assert bufs[0]["flag_r"][0].item() == 1 and bufs[1]["flag_r"][0].item() == 1
+    err.zero_()
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0
+
+
 def test_p2p_wait_gives_up_and_reports():
     """A flag nothing sets: the bounded wait ends after its budget with the
     error code in the error word, and the stream stays usable."""
