@@ -62,11 +62,18 @@ def parse():
                     help="decode: separate fetch and gate/up launches")
     ap.add_argument("--fetch-ctas", type=int, default=0)
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
-    ap.add_argument("--cpu-layers", type=int, default=4)
+    ap.add_argument("--cpu-layers", type=int, default=8,
+                    help="decode CPU legs: layers per sampled token (time scaled to --layers)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--e2e-steps", type=int, default=0,
+                    help="decode: end-to-end steps (0 = --steps, the timed window)")
+    ap.add_argument("--cache-warm-steps", type=int, default=512,
+                    help="decode: graph replays that bring the caches to steady state "
+                         "before --warmup")
     ap.add_argument("--ep-exchange", choices=("p2p", "nccl"), default="p2p",
                     help="ep workload: NVLink peer stores or NCCL all-to-all")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="decode: skip the resident expert-parallel sub-record")
     return ap.parse_args()
 
 
@@ -109,10 +116,16 @@ class CpuDecodeSample:
         gen = "cuda" if torch.cuda.is_available() else "cpu"
         g = torch.Generator().manual_seed(seed + 7)
         self.L, self.k, self.trace = layers, trace.shape[2], trace
+        from drama3_offloading_b200 import decode as dec
         if R is None:  # the GPU stack's dense stand-in rows (6.9 GiB with the shared experts)
-            from drama3_offloading_b200.decode import DENSE_GIB
-            per = DENSE_GIB * (1 << 30) / 40 - (3 * inter * hidden + hidden) * 2
-            R = max(128, int(per / (2 * hidden * 2)) // 128 * 128)
+            R = dec.dense_stand_in_rows(40, hidden, inter, dec.DENSE_GIB)
+        # the full-attention layers' 2048-token KV context, as on the GPU
+        self.kv = {l: ((torch.randn(dec.KV_HEADS, dec.KV_CONTEXT, dec.HEAD_DIM, generator=g)
+                        * 0.5).to(torch.bfloat16),
+                       torch.randn(dec.KV_HEADS, dec.KV_CONTEXT, dec.HEAD_DIM, generator=g)
+                       .to(torch.bfloat16))
+                   for l in dec.full_attention_layers(layers)}
+        self.head_dim = dec.HEAD_DIM
         self.ex = [synth.make_experts(experts, hidden, inter, seed=seed + l, device=gen,
                                       chunk=32).to("cpu") for l in range(layers)]
         self.up = [(torch.randn(R, hidden, generator=g) * hidden ** -0.5).to(torch.bfloat16)
@@ -142,6 +155,12 @@ class CpuDecodeSample:
         for l in range(self.L):
             h = self.h
             h = h + torch.nn.functional.silu(h @ self.up[l].t()) @ self.down[l].t()
+            if l in self.kv:
+                kc, vc = self.kv[l]
+                q = h.view(kc.shape[0], -1, self.head_dim)
+                pr = torch.softmax(torch.bmm(q, kc.transpose(1, 2)).float()
+                                   * self.head_dim ** -0.5, dim=-1).to(torch.bfloat16)
+                h = h + 0.25 * torch.bmm(pr, vc).view(1, -1)
             _, w, _, _ = o.router_topk(h, self.gate[l], self.k)
             ys = o.shared_expert_forward(h, *self.shared[l])
             slots, fs, fe, n = o.resolve(self.tabs[l], row[l])
@@ -174,7 +193,7 @@ def cpu_decode_baseline(trace, capacity, layers_total, sample_layers, sample_s) 
             "sample": f"{len(times)} tokens x {sample_layers} of {layers_total} layers (per-token "
                       f"time scaled by {layers_total}/{sample_layers}); torch bf16 dense GEMVs + "
                       f"oracle router/LRU + expert memcpy + dequantised fp32 expert matmuls + "
-                      f"shared expert"}
+                      f"shared expert + KV-context attention on the full-attention layers"}
 
 
 def cpu_fetch_baseline(trace, capacity, sample_s) -> dict:
@@ -212,7 +231,36 @@ def measured_peaks() -> dict:
 
 # ---------------------------------------------------------------- decode
 
+def decode_config(args, capacity: int | None = None) -> dict:
+    """The decode workload's ``config`` (the same dict for both arms)."""
+    from drama3_offloading_b200 import decode as dec
+    cap = capacity or max(1, int(args.cache_gib * (1 << 30)) // (args.layers * EXPERT_BYTES))
+    dense = dec.dense_bytes_per_token(args.layers)
+    return {"workload": "decode-40L-bs1-offloaded", "layers": args.layers, "hidden": 2048,
+            "experts": 256, "topk": 8, "shared_expert": True, "cache_gib": args.cache_gib,
+            "slots_per_layer": cap, "policy": args.policy, "fetch_overlap": not args.no_overlap,
+            "kv_context": dec.KV_CONTEXT,
+            "kv_mib_per_token": len(dec.full_attention_layers(args.layers)) * 2 *
+            dec.KV_CONTEXT * dec.KV_HEADS * dec.HEAD_DIM * 2 / 2**20,
+            "dense_gib_per_token": dense / 2**30,
+            "cache_warm_steps": args.cache_warm_steps,
+            "l2": "inputs > L2 (30 GiB host store, 6.9 GiB dense, 8 GiB cache)",
+            "parallelism": f"replicas{args.gpus}"}
+
+
+# PCIe read bytes per missed expert of the overlapped fetch launch
+# (fetch_gemv13_kernel), from one ncu capture of the 4-layer decode case:
+# pcie__read_bytes.sum of the captured launches / the experts they fetched
+# (profiles/fetch_gemv13_kernel_traffic_decode4L.md).  None = not measured.
+FETCH_PCIE_BYTES_PER_EXPERT = None
+
+
 def run_decode(args, rank, world, local):
+    """configs[2].  After capture the caches are warmed to steady state by
+    ``--cache-warm-steps`` graph replays plus the ``--warmup`` ones; the
+    state at the start of the timed window is then snapshotted, so the end-to-
+    end run and the fetch-kernel timing replay exactly the same window of
+    tokens from exactly the same cache state as the device-timed ``value``."""
     from drama3_offloading_b200 import benchutil
     from drama3_offloading_b200.decode import DecodeStack
 
@@ -229,9 +277,9 @@ def run_decode(args, rank, world, local):
     if args.fetch_ctas > 0:
         devcache.OVERLAP_FETCH_CTAS = args.fetch_ctas
     g = stack.capture()
-    for _ in range(args.warmup):
+    for _ in range(args.cache_warm_steps + args.warmup):
         g.replay()
-    torch.cuda.synchronize(dev)
+    window = stack.snapshot()
     c0 = stack.store.counters()
     benchutil.barrier(world, dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -252,31 +300,37 @@ def run_decode(args, rank, world, local):
     ms_max = benchutil.max_over_ranks(ms, world, dev)
     value = world * args.steps / (ms_max * 1e-3)
 
-    # end to end through the public API: per token, the input hidden state
-    # comes from pinned host memory and the output goes back to it
-    h_in = torch.randn(1, stack.H, dtype=torch.bfloat16).pin_memory()
+    # end to end through the public API, the same window from the same state:
+    # per token the input hidden state comes from pinned host memory and the
+    # output goes back to it before the next token starts
+    e2e_steps = args.e2e_steps or args.steps
+    stack.restore(window)
+    h_in = window["h"].cpu().pin_memory()
     h_out = torch.empty(1, stack.H, dtype=torch.bfloat16).pin_memory()
     torch.cuda.synchronize(dev)
     benchutil.barrier(world, dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.e2e_steps):
+    for _ in range(e2e_steps):
         stack.h.copy_(h_in, non_blocking=True)
         g.replay()
         h_out.copy_(stack.h, non_blocking=True)
         torch.cuda.current_stream().synchronize()
+        h_in.copy_(h_out)
     e1.record()
     torch.cuda.synchronize(dev)
     e2e_ms = benchutil.max_over_ranks(e0.elapsed_time(e1), world, dev)
-    e2e = world * args.e2e_steps / (e2e_ms * 1e-3)
+    e2e = world * e2e_steps / (e2e_ms * 1e-3)
 
-    # fetch kernel bandwidth, measured with events around every layer's
-    # allocator+fetch launch pair over a few eager steps
-    ft = stack.sample_fetch_timing(8)
+    # the fetch launch's bandwidth over the same window again: eager steps
+    # with CUDA events around every layer's fetch launch
+    stack.restore(window)
+    ft = stack.sample_fetch_timing(args.steps)
     fetch_gbs = ft["bytes"] / (ft["ms"] * 1e-3) / 1e9 if ft["ms"] > 0 else 0.0
     hbm = measured_peaks()
     roof_ms = stack.roofline_ms(hits, misses, hbm["hbm_gbs"], peak["gbs"])
-    return {"value": value, "ms": ms_max, "e2e": e2e, "clk": clk.summary(), "peak": peak,
+    return {"value": value, "ms": ms_max, "e2e": e2e, "e2e_steps": e2e_steps,
+            "clk": clk.summary(), "peak": peak,
             "hits": hits, "misses": misses, "fetch_gbs": fetch_gbs, "fetch_sample": ft,
             "roof_ms": roof_ms, "hbm": hbm, "capacity": stack.capacity,
             "launches": stack.launches_per_step() * args.steps, "trace": stack.trace_dev.cpu().numpy(),
@@ -628,6 +682,18 @@ def run_ep(args, rank, world, local):
         torch.cuda.synchronize(dev)
     benchutil.barrier(world, dev)
     ms = benchutil.max_over_ranks(a.elapsed_time(b), world, dev)
+    # the NVLink exchange, timed in one eager step: CUDA events around every
+    # layer's dispatch and combine (the combine's wait for the slowest
+    # serving rank included); max over ranks
+    dispatch_us = combine_us = None
+    if m.p2p is not None:
+        xe = []
+        m.step(xchg_events=xe)
+        torch.cuda.synchronize(dev)
+        dispatch_us = benchutil.max_over_ranks(
+            float(np.mean([d0.elapsed_time(d1) for d0, d1, _, _ in xe])) * 1e3, world, dev)
+        combine_us = benchutil.max_over_ranks(
+            float(np.mean([c0.elapsed_time(c1) for _, _, c0, c1 in xe])) * 1e3, world, dev)
     # the expert call per rank, timed as it runs in the step -- replayed from a
     # CUDA graph with CUDA events -- on the rows this rank received last, for
     # each layer's weights; bytes = the distinct local experts in those rows
@@ -707,7 +773,21 @@ def run_ep(args, rank, world, local):
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "overflow_pairs": overflow, "clocks": clk.summary(),
         "gpu_launches": args.steps * args.layers * per_layer,
+        "exchange_dispatch_us": dispatch_us, "exchange_combine_us": combine_us,
+        "limiter": ep_limiter(ms / args.steps / args.layers * 1e3, gemm_us, dispatch_us,
+                              combine_us),
     }
+
+
+def ep_limiter(layer_us, expert_us, dispatch_us, combine_us) -> str:
+    """Which part of an expert-parallel layer step the time goes to."""
+    parts = {"expert call (route + GEMMs + act + combine-return)": expert_us}
+    if dispatch_us is not None:
+        parts["NVLink dispatch"] = dispatch_us
+        parts["combine incl. wait for the slowest rank"] = combine_us
+    top = max(parts, key=parts.get)
+    return (f"{top}: {parts[top]:.1f} of {layer_us:.1f} us per layer "
+            f"({', '.join(f'{k} {v:.1f}' for k, v in parts.items())})")
 
 
 # ---------------------------------------------------------------- main
@@ -728,18 +808,20 @@ def reference_arm(args, rank):
         cfg = {"workload": "fetch", "layers": args.layers, "slots": args.slots}
     else:
         cap = max(1, int(args.cache_gib * (1 << 30)) // (args.layers * EXPERT_BYTES))
-        cpu = CpuDecodeSample(1, trace, cap)
+        nl = max(1, min(args.layers, args.cpu_layers))
+        cpu = CpuDecodeSample(nl, trace, cap)
         for _ in range(args.warmup):
             cpu.token()
         ts = [cpu.token() for _ in range(args.steps)]
-        v = 1.0 / (float(np.mean(ts)) * args.layers)
-        unit, metric, dtype = "tok/s", METRIC_DECODE, "bf16/fp8"
+        v = 1.0 / (float(np.mean(ts)) / nl * args.layers)
+        unit, metric = "tok/s", METRIC_DECODE
+        dtype = "fp8 weights x bf16 activations (fp32 accumulate), bf16 dense"
         r = {"cores": cpu.threads, "kind": "port",
-             "sample": f"each step: one token through 1 of {args.layers} layers (time x "
-                       f"{args.layers}); torch bf16 dense GEMVs + oracle router/LRU + expert "
-                       f"memcpy + dequantised fp32 expert matmuls"}
-        cfg = {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
-               "cache_gib": args.cache_gib}
+             "sample": f"each step: one token through {nl} of {args.layers} layers (time x "
+                       f"{args.layers}/{nl}); torch bf16 dense GEMVs + KV-context attention + "
+                       f"oracle router/LRU + expert memcpy + dequantised fp32 expert matmuls "
+                       f"+ shared expert"}
+        cfg = decode_config(args)
     line = {"impl": "reference", "metric": metric, "value": v, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
@@ -765,10 +847,18 @@ def main():
             import torch.distributed as dist
             dist.destroy_process_group()
         return
+    ep_rec = None
     if args.workload == "fetch":
         r = run_fetch(args, rank, world, local)
     else:
         r = run_decode(args, rank, world, local)
+        if not args.no_ep:
+            # the resident expert-parallel configuration at the same
+            # N, after the decode stack is gone: a sub-record of the same line
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
+            ep_rec = run_ep(args, rank, world, local)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -796,24 +886,22 @@ def main():
             }
         else:
             tokb = r["value"] / world
+            misses_per_launch = r["misses"] / args.layers
+            traffic = (FETCH_PCIE_BYTES_PER_EXPERT * misses_per_launch
+                       if FETCH_PCIE_BYTES_PER_EXPERT else None)
             line = {
                 "metric": METRIC_DECODE, "value": r["value"], "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "fp8 weights x bf16 activations (fp32 accumulate), bf16 dense",
                 "data": "synthetic (random-init Drama-3 shapes, seeded Zipf(1.1) routing trace)",
-                "config": {"workload": "decode-40L-bs1-offloaded", "layers": args.layers,
-                           "hidden": 2048, "experts": 256, "topk": 8, "shared_expert": True,
-                           "cache_gib": args.cache_gib,
-                           "slots_per_layer": r["capacity"], "policy": args.policy,
-                           "fetch_overlap": not args.no_overlap,
-                           "dense_gib_per_token": r["dense_bytes"] / 2**30,
-                           "l2": "inputs > L2 (30 GiB host store, 6.9 GiB dense, 8 GiB cache)",
-                           "parallelism": f"replicas{world}"},
+                "config": decode_config(args, r["capacity"]),
                 "hits_per_token": r["hits"], "misses_per_token": r["misses"],
                 "hit_rate": r["hits"] / max(1e-9, r["hits"] + r["misses"]),
                 "fetch_gbs": r["fetch_gbs"], "host_link_peak_gbs": peak,
                 "fetch_frac_of_host_peak": r["fetch_gbs"] / peak,
+                "fetch_window": "the timed window again from the same cache state, eager, "
+                                "CUDA events around every layer's fetch launch",
                 "token_roofline_ms": r["roof_ms"],
                 "token_roofline_frac": r["roof_ms"] / (1e3 / tokb),
                 "roofline": {"bound": "host_link",
@@ -822,12 +910,25 @@ def main():
                                         if not args.no_overlap
                                         else "fetch_layer_kernel (+allocator)"),
                              "achieved": r["fetch_gbs"], "peak": peak, "unit": "GB/s",
-                             "frac": r["fetch_gbs"] / peak, "traffic": None,
+                             "frac": r["fetch_gbs"] / peak, "traffic": traffic,
+                             "traffic_unit": "PCIe read bytes per launch (ncu "
+                                             "pcie__read_bytes.sum per fetched expert x "
+                                             "experts fetched per launch in this window)",
+                             "algorithmic_bytes": misses_per_launch * EXPERT_BYTES,
                              "peak_source": "measured pinned copy-engine H2D, this run"},
                 "e2e": {"value": r["e2e"], "unit": "tok/s", "h2d_bytes_per_step": 2 * 2048,
-                        "d2h_bytes_per_step": 2 * 2048},
+                        "d2h_bytes_per_step": 2 * 2048,
+                        "window": f"the timed window from the same state ({r['e2e_steps']} "
+                                  "steps), host sync every token"},
                 "clocks": r["clk"], "gpu_launches": r["launches"],
             }
+        if ep_rec is not None:
+            line["ep"] = {k: ep_rec[k] for k in (
+                "metric", "value", "unit", "n_gpus", "ms_per_step", "expert_call_us",
+                "exchange_dispatch_us", "exchange_combine_us", "limiter", "overflow_pairs",
+                "gpu_launches", "config")}
+            line["ep"]["roofline"] = {k: ep_rec["roofline"][k] for k in (
+                "bound", "achieved", "peak", "unit", "frac", "per_rank_gbs", "bytes")}
         line["cpu_baseline"] = None if cpu is None else {
             k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)

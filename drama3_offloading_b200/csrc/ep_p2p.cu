@@ -42,6 +42,10 @@
 
 namespace d3 {
 
+// Pairs one dispatch call takes (the decode batches of the expert-parallel
+// configuration route 64-512 pairs per rank).
+constexpr int kP2pDispatchMaxPairs = 4096;
+
 struct P2pDispatchParams {
   const int32_t* ids;
   int T, topk, n_ranks, rank, epr, cap;
@@ -225,8 +229,14 @@ int d3_ep_dispatch_p2p(const void* x, const int32_t* ids, int32_t T, int32_t top
   D3_CHECK_ARG(x && ids && peer_recv_x && peer_recv_eid && peer_flag_d && src_slot && overflow &&
                    epoch && counter,
                "d3_ep_dispatch_p2p: null pointer");
-  D3_CHECK_ARG(T >= 1 && topk >= 1 && topk <= 64 && (long)T * topk <= 65536,
-               "T, topk out of range");
+  D3_CHECK_ARG(T >= 1 && topk >= 1 && topk <= 64, "T, topk out of range");
+  // every CTA scans all pairs for its stable rank (P^2 id loads): fine for
+  // decode batches, so larger batches are refused rather than run slowly
+  if ((long)T * topk > kP2pDispatchMaxPairs)
+    return fail(D3_ERR_TOO_LARGE,
+                "d3_ep_dispatch_p2p: T*topk = %ld exceeds %d (use d3_ep_dispatch_pack and an "
+                "all-to-all for larger batches)",
+                (long)T * topk, kP2pDispatchMaxPairs);
   D3_CHECK_ARG(H >= 8 && H % 8 == 0, "H must be a positive multiple of 8");
   if (n_ranks < 1 || n_ranks > kP2pMaxRanks)
     return fail(D3_ERR_TOO_LARGE, "n_ranks must be in [1, %d]", kP2pMaxRanks);

@@ -490,7 +490,11 @@ int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t H, int3
 // its cache to all free VRAM, bin/offload.py:611-661).  Its scratch -- the
 // per-token-tile arrival counters and the logits -- lives in the file-scope
 // array below, reserved once per GPU when the library's device code is loaded
-// and kept until the process exits.
+// and kept until the process exits.  The first call on a device does a
+// one-time set-up (looks the array's device address up, zeroes its counters
+// with a synchronous memset), so it belongs before any stream capture on that
+// device.  Every call shares the one array: calls that overlap on the GPU
+// (two streams, concurrent graph replays) race and must be serialised.
 
 namespace d3 {
 
@@ -503,7 +507,11 @@ static __device__ __align__(256) unsigned char g_router_scratch[kNoAllocScratchB
 
 // Device address of g_router_scratch on the current device.  The name is only
 // a host-side stand-in in host code, so the address is looked up once per
-// device (with that device current) and cached.
+// device (with that device current) and cached.  The same one-time set-up
+// zeroes the arrival counters (a synchronous memset, before any call on that
+// device can have used them); from then on every launch of the general
+// kernel leaves the counters of the tiles it used at zero again, exactly as
+// with a caller workspace, so no call clears them.
 static int noalloc_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};
@@ -515,6 +523,8 @@ static int noalloc_scratch(void** out) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_router_scratch)");
+    e = cudaMemset(p, 0, kNoAllocCounterBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "clear the router scratch counters");
     addr[dev] = p;
   }
   *out = addr[dev];
@@ -547,12 +557,9 @@ int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  // The arrival counters must start at zero; clear the ones this call uses
-  // (a memset on the stream, no allocation).
-  const size_t tiles = (size_t)(T + kRouterTokensPerCta - 1) / kRouterTokensPerCta;
-  if (T > kRouterClusterMaxT)  // the cluster kernel uses no scratch
-    D3_CUDA_TRY(cudaMemsetAsync(scratch, 0, tiles * sizeof(unsigned), st),
-                "clear router scratch counters");
+  // The arrival counters are zero here: the set-up cleared them and every
+  // launch returns the ones it used to zero (the cluster kernel, T <= 2,
+  // uses no scratch at all).
   RouterParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.w = static_cast<const __nv_bfloat16*>(gate_w);

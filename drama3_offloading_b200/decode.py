@@ -20,6 +20,13 @@ Per layer and decode token (batch 1):
    (``overlap=False``: ``d3_resolve_fetch``, then ``d3_moe_fp8_forward_shared``
    on the cache slots.)
 
+Drama-3's ten full-attention layers (``layer_types``: every fourth layer,
+notes/drama3-config.json; 2 KV heads x 256 dims) also read a 2048-token KV
+context per decode token: 4 MiB per such layer, 40 MiB per token.  The stand-in
+attends the layer's hidden state (as 2 KV groups x 4 query rows) over a
+resident bf16 K/V cache of that size with two batched GEMVs and a softmax
+(cuBLAS / torch), so those bytes are read every token too.
+
 Routing: the router runs every layer (its cost is real), but the expert ids
 fed to the cache come from the seeded Zipf(1.1) trace so hit rates are those
 of skewed real routing rather than of a random-init gate (which routes almost
@@ -37,6 +44,31 @@ from . import _lib, devcache, moe
 from .stack import OffloadedExperts
 
 DENSE_GIB = 6.9
+KV_CONTEXT = 2048        # cached tokens of every full-attention layer
+KV_HEADS, HEAD_DIM = 2, 256
+
+
+def full_attention_layers(layers: int) -> list:
+    """Drama-3's layer_types: layers 3, 7, 11, ... are full attention."""
+    return [l for l in range(layers) if l % 4 == 3]
+
+
+def dense_stand_in_rows(layers: int, hidden: int, inter: int, dense_gib: float) -> int:
+    """Rows R of each layer's up [R, H] / down [H, R] bf16 stand-in: the
+    layer's share of the dense budget minus its shared expert."""
+    shared_bytes = (3 * inter * hidden + hidden) * 2
+    per_layer = dense_gib * (1 << 30) / layers - shared_bytes
+    return max(128, int(per_layer / (2 * hidden * 2)) // 128 * 128)
+
+
+def dense_bytes_per_token(layers: int = 40, hidden: int = 2048, inter: int = 512,
+                          dense_gib: float = DENSE_GIB, kv_context: int = KV_CONTEXT) -> int:
+    """bf16 bytes the non-routed part of one decode token reads: the dense
+    stand-in, the shared experts and the full-attention layers' KV context."""
+    R = dense_stand_in_rows(layers, hidden, inter, dense_gib)
+    shared_bytes = (3 * inter * hidden + hidden) * 2
+    kv = len(full_attention_layers(layers)) * 2 * kv_context * KV_HEADS * HEAD_DIM * 2
+    return layers * (2 * R * hidden * 2 + shared_bytes) + kv
 
 
 class DecodeStack:
@@ -44,7 +76,8 @@ class DecodeStack:
                  topk: int = 8, cache_gib: float = 8.0, capacity: int | None = None,
                  dense_gib: float = DENSE_GIB, trace: np.ndarray | None = None, device="cuda",
                  policy: str = "lru", seed: int = 0, fill: str = "random", group=None,
-                 local_rank: int = 0, trace_offset: int = 0, overlap: bool = True):
+                 local_rank: int = 0, trace_offset: int = 0, overlap: bool = True,
+                 kv_context: int = KV_CONTEXT):
         self.device = dev = torch.device(device)
         self.overlap = overlap
         self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
@@ -64,15 +97,23 @@ class DecodeStack:
                        for _ in range(layers)]
         shared_bytes = (3 * inter * hidden + hidden) * 2
         # dense stand-in: 2 * R * H bf16 per layer
-        per_layer = dense_gib * (1 << 30) / layers - shared_bytes
-        R = max(128, int(per_layer / (2 * hidden * 2)) // 128 * 128)
+        R = dense_stand_in_rows(layers, hidden, inter, dense_gib)
         self.R = R
         self.up = [torch.randn(R, hidden, generator=g, device=dev, dtype=torch.bfloat16) * (hidden ** -0.5)
                    for _ in range(layers)]
         self.down = [torch.randn(hidden, R, generator=g, device=dev, dtype=torch.bfloat16) * (R ** -0.5 * 0.5)
                      for _ in range(layers)]
+        # the full-attention layers' KV context: K and V [KV_HEADS, ctx, HEAD_DIM]
+        self.kv_context = kv_context
+        self.kv = {}
+        if kv_context > 0 and hidden % (KV_HEADS * HEAD_DIM) == 0:
+            for l in full_attention_layers(layers):
+                k = torch.randn(KV_HEADS, kv_context, HEAD_DIM, generator=g, device=dev) * 0.5
+                v = torch.randn(KV_HEADS, kv_context, HEAD_DIM, generator=g, device=dev)
+                self.kv[l] = (k.to(torch.bfloat16), v.to(torch.bfloat16))
+        self.kv_bytes = sum(k.numel() * 2 + v.numel() * 2 for k, v in self.kv.values())
         self.dense_bytes = (sum(t.numel() * 2 for t in self.up + self.down) +
-                            layers * shared_bytes)
+                            layers * shared_bytes + self.kv_bytes)
         self.gate = [(torch.randn(experts, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
                      for _ in range(layers)]
         self.h = torch.zeros(1, hidden, dtype=torch.bfloat16, device=dev)
@@ -96,6 +137,14 @@ class DecodeStack:
         h = self.h
         a = torch.nn.functional.silu(h @ self.up[l].t())
         h.addmm_(a, self.down[l].t())
+        kv = self.kv.get(l)
+        if kv is not None:
+            # decode attention over the cached context: q [groups, rows, d]
+            k, v = kv
+            q = h.view(KV_HEADS, -1, HEAD_DIM)
+            p = torch.softmax(torch.bmm(q, k.transpose(1, 2)).float() * HEAD_DIM ** -0.5,
+                              dim=-1).to(torch.bfloat16)
+            h.add_(torch.bmm(p, v).view(1, -1), alpha=0.25)
         moe.router_topk(h, self.gate[l], self.k, out_ids=self.ids, out_w=self.wts)
         ex = self.store.layers[l]
         if events is not None:
@@ -145,6 +194,30 @@ class DecodeStack:
         self.graph = g
         self.reset()
         return g
+
+    _TABLES = ("_dc_slot_of", "_dc_slot_expert", "_dc_stamp", "_dc_step", "_dc_freq",
+               "_dc_ins", "_dc_out", "_dc_fslot", "_dc_fexp", "_dc_nmiss", "_dc_counters",
+               "_dc_w13", "_dc_w2", "_dc_s13", "_dc_s2")
+
+    def snapshot(self) -> dict:
+        """A device copy of everything a replay changes -- every layer's slot
+        tables, job table, counters and cache bytes, the hidden state and the
+        trace position -- so the same window of tokens can be run again from
+        the same state (``restore``)."""
+        torch.cuda.synchronize(self.device)
+        return {"layers": [[getattr(ex, n).clone() for n in self._TABLES]
+                           for ex in self.store.layers],
+                "h": self.h.clone(), "step_idx": self.step_idx.clone()}
+
+    def restore(self, snap: dict) -> None:
+        """Copy a ``snapshot`` back in place (addresses unchanged, so captured
+        graphs stay valid)."""
+        for ex, saved in zip(self.store.layers, snap["layers"]):
+            for n, t in zip(self._TABLES, saved):
+                getattr(ex, n).copy_(t)
+        self.h.copy_(snap["h"])
+        self.step_idx.copy_(snap["step_idx"])
+        torch.cuda.synchronize(self.device)
 
     def reset(self) -> None:
         """Cold caches, trace at its start, zero hidden state (addresses unchanged)."""

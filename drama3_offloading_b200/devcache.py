@@ -99,7 +99,8 @@ def init_dev_cache(experts, device: torch.device, capacity: int, policy: str | N
                                  dtype=torch.float32, device=device)
     experts._dc_s2 = torch.ones((capacity, *experts.w2_scale_inv.shape[1:]),
                                 dtype=torch.float32, device=device)
-    # scratch, allocated once so nothing allocates inside a captured region
+    # per-call result and job tables live here for the layer's lifetime: a
+    # resolve call writes into them and never allocates, so it can be captured
     experts._dc_out = torch.zeros(K_MAX, dtype=torch.int32, device=device)
     experts._dc_fslot = torch.zeros(K_MAX, dtype=torch.int32, device=device)
     experts._dc_fexp = torch.zeros(K_MAX, dtype=torch.int32, device=device)

@@ -19,6 +19,14 @@ Every buffer has a fixed shape (capacity = local pairs per peer), so the step
 needs no host sync and is captured into one CUDA graph, collectives included.
 At N = 1 the exchange disappears and the layer is one fp8_moe_forward.
 
+Errors: every NVLink wait is bounded (2 s of GPU time).  A wait that runs out
+records a code in the device error word and the step goes on -- it cannot
+stop mid-graph -- so that step's hidden states are wrong.  The step itself
+never reads the word (that would sync the host every step): call
+``check()`` (or ``moe.check_errors()``) after ``step()`` or after replaying
+the captured graph, or pass ``step(check=True)``; ``close()`` checks once
+more and raises after tearing the exchange down.
+
 No counterpart in the reference (it has no multi-GPU code).
 """
 from __future__ import annotations
@@ -144,7 +152,8 @@ class ExpertParallelMoE:
         moe.router_topk(self.h, self.gate[0], topk, out_ids=self.ids, out_w=self.wts)
 
     # ------------------------------------------------------------ one step
-    def _layer(self, l: int, ids: torch.Tensor, gemm_events: list | None = None) -> None:
+    def _layer(self, l: int, ids: torch.Tensor, gemm_events: list | None = None,
+               xchg_events: list | None = None) -> None:
         h = self.h
         moe.router_topk(h, self.gate[l], self.k, out_ids=self.ids, out_w=self.wts)
         w = self.w[l]
@@ -160,7 +169,7 @@ class ExpertParallelMoE:
             return
         st = _lib.stream_ptr()
         if self.p2p is not None:
-            self._layer_p2p(l, ids, w, st, gemm_events)
+            self._layer_p2p(l, ids, w, st, gemm_events, xchg_events)
             return
         _lib.call("d3_ep_dispatch_pack", _lib.ptr(h), _lib.ptr(ids), self.T, self.k, self.H,
                   self.world, self.epr, self.cap, _lib.ptr(self.send_x), _lib.ptr(self.send_eid),
@@ -181,18 +190,25 @@ class ExpertParallelMoE:
 
     WAIT_BUDGET_NS = 2_000_000_000
 
-    def _layer_p2p(self, l, ids, w, st, gemm_events) -> None:
+    def _layer_p2p(self, l, ids, w, st, gemm_events, xchg_events=None) -> None:
         """The same layer with the exchange over NVLink peer stores, in three C
         calls: the dispatch stores the rows into the peers; the expert call
         waits for every source's rows (in its route launch) and stores each
         served row back into its source (in its combine launch); the combine
-        waits for every serving rank's rows."""
+        waits for every serving rank's rows.  ``xchg_events`` receives CUDA
+        event pairs around the dispatch and around the combine (its wait for
+        the slowest serving rank included)."""
         x = self.p2p
         err = moe.error_word(self.device)
+        if xchg_events is not None:
+            d0, d1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            d0.record()
         _lib.call("d3_ep_dispatch_p2p", _lib.ptr(self.h), _lib.ptr(ids), self.T, self.k, self.H,
                   self.world, self.rank, self.epr, self.cap, x.peer["recv_x"],
                   x.peer["recv_eid"], x.peer["flag_d"], _lib.ptr(self.src_slot),
                   _lib.ptr(self.overflow), _lib.ptr(x.epoch), _lib.ptr(x.counters), st)
+        if xchg_events is not None:
+            d1.record()
         if gemm_events is not None:
             e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
             e0.record()
@@ -205,26 +221,50 @@ class ExpertParallelMoE:
         if gemm_events is not None:
             e1.record()
             gemm_events.append((e0, e1))
+        if xchg_events is not None:
+            c0, c1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            c0.record()
         _lib.call("d3_ep_combine_p2p", _lib.ptr(x.ret), _lib.ptr(self.src_slot),
                   _lib.ptr(self.wts), 1, self.T, self.k, self.H, _lib.ptr(self.h), 1,
                   _lib.ptr(x.flag_r), self.world, _lib.ptr(x.epoch), _lib.ptr(err), 32,
                   self.WAIT_BUDGET_NS, st)
+        if xchg_events is not None:
+            c1.record()
+            xchg_events.append((d0, d1, c0, c1))
+
+    def check(self) -> None:
+        """Raise if a bounded NVLink wait of an earlier step ran out (reads the
+        device error word: synchronises the host with the device)."""
+        moe.check_errors(self.device)
 
     def close(self) -> None:
-        """Unmap the peers' exchange buffers (after the last step, on every rank)."""
+        """Unmap the peers' exchange buffers (after the last step, on every
+        rank), then raise if any step's bounded wait ran out."""
         torch.cuda.synchronize(self.device)
+        code = int(moe.error_word(self.device).item())
         self.graph = None
         if self.p2p is not None:
             import torch.distributed as dist
             dist.barrier(group=self.group)
             self.p2p.close()
             self.p2p = None
+        if code:
+            raise RuntimeError(f"d3 device error code {code}: {moe.error_message(code)} "
+                               "(a bounded wait expired during an earlier step)")
 
-    def step(self, gemm_events: list | None = None) -> None:
+    def step(self, gemm_events: list | None = None, check: bool = False,
+             xchg_events: list | None = None) -> None:
+        """One decode step of all layers (eager; capturable).  ``check=True``
+        synchronises afterwards and raises if a bounded wait ran out (not
+        inside a capture).  The event lists (eager timing only) receive CUDA
+        event pairs around each layer's expert call, and around its NVLink
+        dispatch and combine."""
         cur = self.trace_dev.index_select(0, self.step_idx)[0]
         self.step_idx.add_(1).remainder_(self.trace_steps)
         for l in range(self.L):
-            self._layer(l, cur[l], gemm_events)
+            self._layer(l, cur[l], gemm_events, xchg_events)
+        if check:
+            self.check()
 
     def capture(self) -> torch.cuda.CUDAGraph:
         s = torch.cuda.Stream(device=self.device)

@@ -224,45 +224,81 @@ def offloaded_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
     return moe.fp8_moe_forward(x, local, topk_weights, b["w13"], b["s13"], b["w2"], b["s2"])
 
 
-def pin_experts(model, device=None) -> tuple[float, float]:
-    """Page-lock the CPU-resident expert buffers (bin/offload.py:664-699).
-    Returns (GiB, seconds)."""
-    started = time.perf_counter()
+def offloaded_stores(source) -> list:
+    """The expert stores that live in host memory.  ``source`` is a model in
+    the reference's layout (``model.backbone.model.layers[i].mlp.experts``:
+    layers without an ``experts`` store, or whose store already sits on a
+    GPU, are skipped) or any iterable of stores (``HostExperts``,
+    ``OffloadedExperts.layers``)."""
+    backbone = getattr(source, "backbone", None)
+    if backbone is not None:
+        found = (getattr(getattr(layer, "mlp", None), "experts", None)
+                 for layer in backbone.model.layers)
+    else:
+        found = iter(source)
+    return [ex for ex in found if ex is not None and ex.w13_weight.device.type == "cpu"]
+
+
+def bytes_per_expert(experts) -> int:
+    """Bytes one expert occupies over its four buffers (weights and scales),
+    measured from the store itself -- the unit a cache slot holds."""
+    from .devcache import _BUFFERS
     total = 0
-    for layer in model.backbone.model.layers:
-        experts = getattr(layer.mlp, "experts", None)
-        if experts is None or experts.w13_weight.device.type != "cpu":
-            continue
-        for name in ("w13_weight", "w2_weight", "w13_scale_inv", "w2_scale_inv"):
-            buf = getattr(experts, name)
-            if buf.is_pinned():
-                continue
-            pinned = buf.pin_memory()
-            setattr(experts, name, pinned)
-            total += pinned.numel() * pinned.element_size()
-    return total / 2**30, time.perf_counter() - started
+    for name in _BUFFERS:
+        t = getattr(experts, name)
+        total += t.numel() * t.element_size() // experts.num_experts
+    return total
+
+
+def pin_experts(model, device=None) -> tuple[float, float]:
+    """Page-lock every host expert buffer that is not page-locked yet
+    (the reference's ``pin_experts``, bin/offload.py:664-699: same arguments,
+    same (GiB newly pinned, seconds) result).  Buffers are replaced one at a
+    time by a pinned copy, so the transient extra host memory is one buffer.
+    ``model`` may also be an iterable of expert stores.  (The decode stack here
+    uses ``hoststore.SharedHostStore`` instead: one page-locked copy per
+    machine, registered in place.)"""
+    from .devcache import _BUFFERS
+    t0 = time.perf_counter()
+    todo = [(ex, name) for ex in offloaded_stores(model) for name in _BUFFERS
+            if not getattr(ex, name).is_pinned()]
+    pinned_bytes = 0
+    for ex, name in todo:
+        locked = getattr(ex, name).pin_memory()
+        setattr(ex, name, locked)
+        pinned_bytes += locked.numel() * locked.element_size()
+    return pinned_bytes / 2**30, time.perf_counter() - t0
 
 
 def size_cache_to_free_vram(model, device, leave_free_gib: float = 2.0,
                             cap_per_layer: int = 256) -> int:
-    """Per-layer device-cache capacity from the memory free right now
-    (bin/offload.py:611-661); allocates the caches and returns the capacity."""
+    """Give the device memory that is free right now, minus a reserve, to the
+    expert caches of every offloaded layer, evenly (the reference's
+    ``size_cache_to_free_vram``, bin/offload.py:611-661: same arguments and
+    result).  The reserve is ``leave_free_gib`` for other programs plus
+    ``ACTIVATION_HEADROOM_GIB`` for this process's own decode peak.  The
+    allocator's idle blocks are released first so they count as free.  The
+    slot size is measured from the stores (``bytes_per_expert``), and the
+    capacity is clamped to ``cap_per_layer`` and to the layer's expert count.
+    Allocates the caches (``devcache.init_dev_cache``) and returns the
+    per-layer capacity; 0 (nothing allocated) when the budget does not hold
+    one slot per layer."""
     from . import devcache
-    layers = [l.mlp.experts for l in model.backbone.model.layers
-              if getattr(l.mlp, "experts", None) is not None
-              and l.mlp.experts.w13_weight.device.type == "cpu"]
-    if not layers:
+    stores = offloaded_stores(model)
+    if not stores:
         return 0
+    device = torch.device(device)
     torch.cuda.synchronize(device)
     torch.cuda.empty_cache()
-    free, _ = torch.cuda.mem_get_info(device)
-    budget = free - int((leave_free_gib + ACTIVATION_HEADROOM_GIB) * 2**30)
-    capacity = int(max(0, budget) // (len(layers) * EXPERT_BYTES))
-    capacity = min(capacity, cap_per_layer, layers[0].num_experts)
-    if capacity <= 0:
+    free_bytes = torch.cuda.mem_get_info(device)[0]
+    reserve = int((leave_free_gib + ACTIVATION_HEADROOM_GIB) * 2**30)
+    slot_row = sum(bytes_per_expert(ex) for ex in stores)   # one slot in every layer
+    fits = max(0, free_bytes - reserve) // slot_row
+    capacity = int(min(fits, cap_per_layer, min(ex.num_experts for ex in stores)))
+    if capacity < 1:
         return 0
-    for experts in layers:
-        devcache.init_dev_cache(experts, device, capacity)
+    for ex in stores:
+        devcache.init_dev_cache(ex, device, capacity)
     return capacity
 
 

@@ -219,7 +219,8 @@ D3_API int d3_router_topk(const void* x, const void* gate_w, int32_t T, int32_t 
  * every GPU that loads it until the process exits.  Limits: T <= 2048 and
  * T * E <= 65536 (e.g. T = 256 at E = 256); larger calls return
  * D3_ERR_TOO_LARGE.  The first call on each device looks the array's device
- * address up, so make it before any stream capture on that device.  All
+ * address up and zeroes its counters (a synchronous memset), so make it
+ * before any stream capture on that device.  All
  * calls share the one array, so calls that overlap on the GPU (different
  * streams, or concurrent graphs) race: serialise them. */
 D3_API int d3_router_topk_noalloc(const void* x, const void* gate_w, int32_t T, int32_t H,
@@ -311,7 +312,9 @@ D3_API int d3_ipc_close(void* base);
  * peer_recv_eid[d]: rows [rank*cap, (rank+1)*cap) belong to this source),
  * then flag_d[rank] = epoch is released on every destination (*epoch is a
  * device counter this call increments once).  counter: a device uint32 that
- * is zero between calls.  n_ranks <= 16.  No counterpart in the reference. */
+ * is zero between calls.  n_ranks <= 16; T * topk <= 4096 (D3_ERR_TOO_LARGE
+ * beyond: larger batches take d3_ep_dispatch_pack and an all-to-all).  No
+ * counterpart in the reference. */
 D3_API int d3_ep_dispatch_p2p(const void* x, const int32_t* ids, int32_t T, int32_t topk,
                               int32_t H, int32_t n_ranks, int32_t rank,
                               int32_t experts_per_rank, int32_t cap, void* const* peer_recv_x,

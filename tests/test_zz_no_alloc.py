@@ -18,6 +18,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from conftest import cuda_available
 
 pytestmark = [pytest.mark.gpu,
@@ -54,11 +55,18 @@ def _noalloc(x, gw, k):
 
 
 def test_noalloc_router_matches_workspace_router_twice():
+    """Every router kernel through the fixed scratch, calls back to back:
+    T = 1, 2 (the cluster kernel, no scratch), 3 and 16 (4-warp split), 64
+    (unsplit general kernel) and 256 at E = 256 (T * E = 65536: the logits
+    fill the whole array, its last element included), then T = 16 again.
+    Each call must equal the workspace router (ids exactly, weights within
+    the router tests' tolerance) and the CPU oracle's ids and weights."""
     g = torch.Generator().manual_seed(99)
-    gw = (torch.randn(256, 2048, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
-    # two calls in a row with different token counts and inputs
-    for T in (16, 3):
-        x = torch.randn(T, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    gw_c = (torch.randn(256, 2048, generator=g) * 0.02).to(torch.bfloat16)
+    gw = gw_c.to(DEV)
+    for T in (1, 2, 3, 16, 64, 256, 16):
+        x_c = torch.randn(T, 2048, generator=g).to(torch.bfloat16)
+        x = x_c.to(DEV)
         want_ids, want_w = _with_workspace(x, gw, 8)
         ids, w, wb = _noalloc(x, gw, 8)
         torch.cuda.synchronize()
@@ -66,6 +74,9 @@ def test_noalloc_router_matches_workspace_router_twice():
         np.testing.assert_allclose(w.cpu().numpy(), want_w.cpu().numpy(), rtol=1e-5, atol=1e-7)
         np.testing.assert_array_equal(wb.float().cpu().numpy(),
                                       want_w.to(torch.bfloat16).float().cpu().numpy())
+        ref_ids, ref_w, _, _ = oracle.router_topk(x_c, gw_c, 8)
+        np.testing.assert_array_equal(ids.cpu().numpy(), ref_ids.numpy())
+        np.testing.assert_allclose(w.cpu().numpy(), ref_w.numpy(), rtol=1e-5, atol=1e-7)
 
 
 def test_noalloc_router_rejects_oversize():
