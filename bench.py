@@ -250,9 +250,11 @@ def decode_config(args, capacity: int | None = None) -> dict:
 
 # PCIe read bytes per missed expert of the overlapped fetch launch
 # (fetch_gemv13_kernel), from one ncu capture of the 4-layer decode case:
-# pcie__read_bytes.sum of the captured launches / the experts they fetched
-# (profiles/fetch_gemv13_kernel_traffic_decode4L.md).  None = not measured.
-FETCH_PCIE_BYTES_PER_EXPERT = None
+# pcie__read_bytes.sum of the 16 captured launches (120,489,472 B) / the 35
+# experts they fetched (profiles/fetch_gemv13_kernel_traffic_decode4L.md):
+# 1.094 x the 3,146,496 algorithmic bytes (the 12-byte completion header of
+# every 128-byte read request counts as read traffic).
+FETCH_PCIE_BYTES_PER_EXPERT = 3_442_556
 
 
 def run_decode(args, rank, world, local):
