@@ -41,6 +41,7 @@ namespace d3 {
 
 constexpr int kGemvThreads = 256;                 // 8 warps
 constexpr int kGemvRowsPerCta = kGemvThreads / 32;
+constexpr int kGemvMaxKbI = 16;                   // I / 128 for I <= 2048 (CPL <= 4)
 
 struct GemvParams {
   const __nv_bfloat16* x;   // [T, H]
@@ -66,6 +67,12 @@ struct GemvParams {
   // after it (0: the preceding launch may still be writing W2, as the fetch +
   // gate/up overlap launch does)
   int w2_early;
+  // with w2_early == 0: the job table of that preceding fetch (the slots
+  // whose W2/S2 bytes it writes; written by the allocator launch before it,
+  // so readable before the wait) -- every other pair's W2 rows and scales
+  // are loaded early; null = none early
+  const int32_t* fetch_slot;
+  const int32_t* nmiss;
 };
 
 // Fetch + gate/up overlap: which queued fetch job (if any) fills each pair's
@@ -260,30 +267,72 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv13_kernel(GemvParams p) 
 // 16-float chunk padded to 20 floats (conflict-free 16-byte reads: lane l's
 // chunk starts at bank 20 l).
 template <int CPL>
-__global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, int rpw) {
+__global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p, int rpw) {
   constexpr int kGemvPairGroup = 8 / CPL;  // W2 rows (of pairs) a warp keeps in flight
   extern __shared__ __align__(16) float s_h[];   // [topk][I / 16][20]
   __shared__ float s_w[64];
   __shared__ int s_e[64];
+  // the W2 block scales of this CTA's rows (all in one 128-row block) per pair
+  __shared__ float s_sc[64][kGemvMaxKbI];
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int I = p.I, H = p.H, topk = p.topk, nkbI = I / 128;
   const int t = blockIdx.y;
   const int row_stride = I / 16 * 20;
   const int j_first = (blockIdx.x * rpw) * kGemvRowsPerCta + warp;
-  // ids were written before the gate/up launch started: safe to read early
+  // ids (and the overlap path's job table) were written before the gate/up
+  // launch started: safe to read early.  A pair is "early" when nothing in
+  // flight writes its slot's W2/S2 bytes: its first W2 row and scales are
+  // loaded before griddepcontrol.wait, so they stream in while the gate/up
+  // products finish.
   int my_e = -1;
-  if (lane < topk) my_e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + lane, p.n);
+  bool my_early = false;
+  if (lane < topk) {
+    my_e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + lane, p.n);
+    my_early = p.w2_early != 0;
+    if (!my_early && my_e >= 0 && p.fetch_slot) {
+      const int nm = __ldcg(p.nmiss);
+      bool fetched = false;
+      for (int jj = 0; jj < nm; ++jj) fetched |= __ldcg(p.fetch_slot + jj) == my_e;
+      my_early = !fetched;
+    }
+  }
+  const unsigned early = __ballot_sync(0xffffffffu, my_early);
   uint4 w0[kGemvPairGroup][CPL];
 #pragma unroll
   for (int q = 0; q < kGemvPairGroup; ++q) {
     const int e = __shfl_sync(0xffffffffu, my_e, q);
-    if (p.w2_early && q < topk && e >= 0 && j_first < H) {
+    if (((early >> q) & 1u) && q < topk && e >= 0 && j_first < H) {
       const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
     }
   }
+  // scales: entry (k, kb) of s_sc = s2[e_k][row block][kb] (this CTA's rows
+  // all lie in one 128-row block), loaded early for early pairs
+  const int rb = (blockIdx.x * rpw * kGemvRowsPerCta) / 128;
+  auto stage_scales = [&](bool want_early) {
+    for (int i = threadIdx.x; i < topk * nkbI; i += blockDim.x) {
+      const int k = i / nkbI, kb = i - k * nkbI;
+      const int e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + k, p.n);
+      if (e < 0) continue;
+      bool is_early = p.w2_early != 0;
+      if (!is_early && p.fetch_slot) {
+        const int nm = __ldcg(p.nmiss);
+        bool fetched = false;
+        for (int jj = 0; jj < nm; ++jj) fetched |= __ldcg(p.fetch_slot + jj) == e;
+        is_early = !fetched;
+      }
+      if (is_early == want_early)
+        s_sc[k][kb] = __ldcg(p.s2 + ((size_t)e * (H / 128) + rb) * nkbI + kb);
+    }
+  };
+  stage_scales(true);
+  // the residual this warp's first output row adds to (not written by this
+  // call's earlier launches)
+  float res0 = 0.f;
+  if (p.accumulate && lane == 0 && j_first < H)
+    res0 = __bfloat162float(p.out[(size_t)t * H + j_first]);
   // the shared expert's first down row too (bf16: two 16-byte words per chunk)
   uint4 sw0[CPL][2];
   if (p.sw13 && j_first < H) {
@@ -295,6 +344,18 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
     }
   }
   pdl_wait();
+  // the first group's remaining W2 rows and scales (slots the preceding launch
+  // wrote), issued before the h staging so both latencies overlap
+#pragma unroll
+  for (int q = 0; q < kGemvPairGroup; ++q) {
+    const int e = __shfl_sync(0xffffffffu, my_e, q);
+    if (!((early >> q) & 1u) && q < topk && e >= 0 && j_first < H) {
+      const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
+    }
+  }
+  stage_scales(false);
   // stage the token's pair rows of h (written by the gate/up launch), and the
   // shared expert's row as row topk
   const int nrows = topk + (p.sw13 ? 1 : 0);
@@ -313,18 +374,36 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
                                            static_cast<const __nv_bfloat16*>(p.weights)[i]);
   }
   __syncthreads();
+  // acc += w[t,k] * s2 * (W2[e_k][j] . h_k) over one group of pairs, k in order
+  auto group = [&](const uint4 (&w)[kGemvPairGroup][CPL], int k0, float acc) {
+#pragma unroll
+    for (int q = 0; q < kGemvPairGroup; ++q) {
+      const int k = k0 + q;
+      const int e = k < topk ? s_e[k] : -1;
+      if (e < 0) continue;
+      float part = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int ch = lane + 32 * c;
+        const float* hp = s_h + k * row_stride + ch * 20;
+        float hv[16];
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+          const float4 a = *reinterpret_cast<const float4*>(hp + 4 * f);
+          hv[4 * f] = a.x; hv[4 * f + 1] = a.y; hv[4 * f + 2] = a.z; hv[4 * f + 3] = a.w;
+        }
+        part = fmaf(s_sc[k][ch >> 3], dot16_e4m3(w[q][c], hv), part);
+      }
+      acc = fmaf(s_w[k], part, acc);
+    }
+    return acc;
+  };
   for (int r = 0; r < rpw; ++r) {
     const int j = j_first + r * kGemvRowsPerCta;
     if (j >= H) break;
     float acc = 0.f;
     for (int k0 = 0; k0 < topk; k0 += kGemvPairGroup) {
-      uint4 w[kGemvPairGroup][CPL];
-      if (r == 0 && k0 == 0 && p.w2_early) {
-#pragma unroll
-        for (int q = 0; q < kGemvPairGroup; ++q)
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) w[q][c] = w0[q][c];
-      } else {
+      if (r > 0 || k0 > 0) {  // the first group's rows are in w0 already
 #pragma unroll
         for (int q = 0; q < kGemvPairGroup; ++q) {
           const int k = k0 + q;
@@ -332,31 +411,11 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
           if (e >= 0) {
             const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j) * I);
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) w[q][c] = __ldcg(wr + lane + 32 * c);
+            for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
           }
         }
       }
-#pragma unroll
-      for (int q = 0; q < kGemvPairGroup; ++q) {
-        const int k = k0 + q;
-        const int e = k < topk ? s_e[k] : -1;
-        if (e < 0) continue;
-        const float* sr = p.s2 + ((size_t)e * (H / 128) + j / 128) * nkbI;
-        float part = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const int ch = lane + 32 * c;
-          const float* hp = s_h + k * row_stride + ch * 20;
-          float hv[16];
-#pragma unroll
-          for (int f = 0; f < 4; ++f) {
-            const float4 a = *reinterpret_cast<const float4*>(hp + 4 * f);
-            hv[4 * f] = a.x; hv[4 * f + 1] = a.y; hv[4 * f + 2] = a.z; hv[4 * f + 3] = a.w;
-          }
-          part = fmaf(__ldcg(sr + (ch >> 3)), dot16_e4m3(w[q][c], hv), part);
-        }
-        acc = fmaf(s_w[k], part, acc);
-      }
+      acc = group(w0, k0, acc);
     }
     if (p.sw13) {  // shared expert: acc += sigmoid gate * (W2s[j] . hs[t])
       uint4 sw[CPL][2];
@@ -388,7 +447,7 @@ __global__ void __launch_bounds__(kGemvThreads) moe_gemv2_kernel(GemvParams p, i
     acc = warp_sum(acc);
     if (lane == 0) {
       __nv_bfloat16* o = p.out + (size_t)t * H + j;
-      if (p.accumulate) acc += __bfloat162float(*o);
+      if (p.accumulate) acc += r == 0 ? res0 : __bfloat162float(*o);
       *o = __float2bfloat16_rn(acc);
     }
   }
