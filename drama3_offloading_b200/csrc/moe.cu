@@ -132,7 +132,9 @@ static void make_plan(Plan& p, int T, int topk, int n, int H, int I, int sms) {
   (void)sms;
   p.maxt1 = nt_bound * (2 * I / 128) * p.split1_max;
   p.maxt2 = nt_bound * (H / 128) * p.split2_max;
-  size_t o = 0;
+  // bytes [0, 256): the one-launch path's grid counter, at the same offset
+  // for every shape so no other data of a reused workspace ever lands there
+  size_t o = 256;
   p.o_cnt = o;     o += al(sizeof(int) * (size_t)n);
   p.o_off = o;     o += al(sizeof(int) * (size_t)n);
   p.o_sorted = o;  o += al(sizeof(int) * (size_t)p.P);
@@ -216,8 +218,9 @@ __device__ __forceinline__ int route_chunk(int P, int nw) {
   return (batches + nw - 1) / nw * 32;
 }
 
-__global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
-  extern __shared__ int sm[];
+// The body, shared by the route launch and the first phase of the fused
+// expert kernel: `sm` is its dynamic shared memory (layout above).
+__device__ __forceinline__ void route_body(const RouteParams& p, int* sm) {
   const int n = p.n, NW = p.nw;
   int* s_cnt = sm;                // [n]
   int* s_off = sm + n;            // [n]
@@ -303,8 +306,11 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   }
   if (lane == 31) { warp_tot[warp] = v; wt2[warp] = w; }
   __syncthreads();
+  // (the CTA may have fewer than 32 warps: entries past the last warp are
+  // not written, and count as zero)
+  const int nwarps = (int)(blockDim.x >> 5);
   if (warp == 0) {
-    int a = warp_tot[lane], b = wt2[lane];
+    int a = lane < nwarps ? warp_tot[lane] : 0, b = lane < nwarps ? wt2[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
@@ -436,6 +442,11 @@ __global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
   }
 }
 
+__global__ void __launch_bounds__(1024) route_kernel(RouteParams p) {
+  extern __shared__ int sm[];
+  route_body(p, sm);
+}
+
 // ---------------------------------------------------------------- 2/4. quantise
 
 // One warp, one 128-wide K block of a pair's token row: 4 values per lane.
@@ -545,6 +556,198 @@ __global__ void __launch_bounds__(256) combine_return_kernel(const float* ws2,
 
 // ---------------------------------------------------------------- 3/5. GEMM
 // (tile engine in gemm_sm100.cuh)
+
+// ---------------------------------------------------------------- one-launch expert call
+//
+// For batches up to kFusedQuantMaxPairs pairs the whole expert call -- route,
+// gate/up GEMM, SwiGLU, down GEMM, combine (or, with the NVLink link, the
+// combine stored into the source ranks plus the return epoch) -- runs as ONE
+// cooperative launch of one CTA per SM, the phases separated by grid-wide
+// barriers on a counter at workspace offset 0:
+//
+//   all threads   route (the stable sort, the tile lists, the quantised
+//                 activations; the stage ring's shared memory is its scratch)
+//   -- barrier 1 (every CTA) --
+//   warp 0        TMA producer: the gate/up tiles, then the down tiles, whose
+//                 weight tiles it issues at once and whose activation tiles
+//                 wait for barrier 3 (the down weights stream into the
+//                 shared-memory ring while SwiGLU runs)
+//   warp 1        MMA issuer: both tile lists through the same rings
+//   epilogue      gate/up tiles -- barrier 2 -- SwiGLU + quantisation units of
+//                 the grid -- barrier 3 -- down tiles -- barrier 4 -- combine
+//                 units -- final arrival (the last CTA publishes the return
+//                 epoch on every source with the NVLink link, and zeroes the
+//                 counter for the next launch)
+//
+// The work and every summation order are those of the separate launches, so
+// the outputs are bit-identical.  No launch boundary separates the phases, so
+// no per-launch ramp and drain sits between them; every wait is bounded
+// (error code 5 for a phase barrier).
+constexpr int kFusedBarrierCode = 5;
+
+struct FusedParams {
+  RouteParams rp;
+  GemmParams g1, g2;
+  int I, H, P, T, topk, weights_f32, accumulate;
+  const float* ws1;
+  uint8_t* hq;
+  float* hs;
+  const float* ws2;
+  const int* inv;
+  const void* weights;
+  __nv_bfloat16* out;
+  unsigned* gbar;          // workspace offset 0, zero between launches
+  int* err;
+  int has_link;
+  P2pLink link;
+};
+
+// The epilogue warps of every CTA meet: named barrier, then one thread
+// arrives on the grid counter and waits (bounded) for `target` arrivals.
+__device__ __forceinline__ void epi_grid_sync(unsigned* gbar, unsigned target, int nepi,
+                                              bool leader, int* err) {
+  epi_bar_sync(nepi);
+  if (leader) {
+    __threadfence();
+    atomicAdd(gbar, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu_u32(gbar) < target) {
+      if (globaltimer_ns() - t0 > kGemmWaitBudgetNs) { gemm_error(err, kFusedBarrierCode); break; }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  epi_bar_sync(nepi);
+}
+
+template <int BN, int KPS>
+__global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
+    moe_fused_kernel(const __grid_constant__ CUtensorMap tw1,
+                     const __grid_constant__ CUtensorMap tx1,
+                     const __grid_constant__ CUtensorMap tw2,
+                     const __grid_constant__ CUtensorMap tx2, const __grid_constant__ FusedParams f) {
+  using Cfg = GemmCfg<BN, KPS>;
+  constexpr int NEPI = 32 * Cfg::EPI;
+  extern __shared__ uint8_t smem_raw[];
+  const GemmSmem<BN, KPS> sm = GemmSmem<BN, KPS>::carve(smem_raw);
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+  __shared__ volatile int s_tile_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned G = gridDim.x;
+  if (threadIdx.x == 0) {
+    sm.init();
+    s_abort = 0;
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tw1);
+    tma_prefetch_desc(&tx1);
+    tma_prefetch_desc(&tw2);
+    tma_prefetch_desc(&tx2);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  // ---- phase 0: route, in the stage ring's memory (no TMA has run yet)
+  route_body(f.rp, reinterpret_cast<int*>(sm.stage_base));
+  fence_proxy_async_global();   // the quantised rows are read by TMA in other CTAs
+  fence_proxy_async_smem();     // the ring's bytes are next written by TMA
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(f.gbar, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu_u32(f.gbar) < G) {
+      if (globaltimer_ns() - t0 > kGemmWaitBudgetNs) { gemm_error(f.err, kFusedBarrierCode); break; }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  const int n1 = __ldcg(f.g1.ntiles), n2 = __ldcg(f.g2.ntiles);
+  PipePos ps;
+  if (warp == 0) {
+    if (lane == 0) {
+      fence_proxy_async_global();
+      gemm_produce<BN, KPS>(sm, &tw1, &tx1, f.g1, n1, ps, &s_abort, nullptr);
+      const OperandGate gate{f.gbar, 3 * G, f.err, kFusedBarrierCode};
+      gemm_produce<BN, KPS>(sm, &tw2, &tx2, f.g2, n2, ps, &s_abort, &gate);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      gemm_mma<BN, KPS>(sm, tmem, f.g1, n1, ps, &s_abort);
+      gemm_mma<BN, KPS>(sm, tmem, f.g2, n2, ps, &s_abort);
+      gemm_mma_drain<BN, KPS>(sm, ps, f.err);
+    }
+  } else {
+    const int ep = threadIdx.x - 64;
+    const bool leader = ep == 0;
+    const long ew = (long)blockIdx.x * Cfg::EPI + (warp - 2), nw = (long)G * Cfg::EPI;
+    gemm_epilogue<BN, KPS>(sm, tmem, f.g1, n1, ps, &s_abort, &s_tile_abort);
+    epi_grid_sync(f.gbar, 2 * G, NEPI, leader, f.err);
+    // ---- SwiGLU + quantisation of h: one warp per (valid sorted row, I block)
+    {
+      const int nvalid = __ldcg(f.rp.ntiles + 2), split1 = __ldcg(f.rp.ntiles + 3);
+      const int nkb = f.I / 128;
+      for (long u = ew; u < (long)nvalid * nkb; u += nw) {
+        const int row = (int)(u / nkb), kb = (int)(u - (long)row * nkb);
+        act_unit(f.ws1, split1, f.P, row, kb, f.I, f.hq, f.hs, lane);
+      }
+      fence_proxy_async_global();   // h is read by TMA in other CTAs
+    }
+    epi_grid_sync(f.gbar, 3 * G, NEPI, leader, f.err);
+    gemm_epilogue<BN, KPS>(sm, tmem, f.g2, n2, ps, &s_abort, &s_tile_abort);
+    epi_grid_sync(f.gbar, 4 * G, NEPI, leader, f.err);
+    // ---- combine: one warp per (token or received row, 128 output columns)
+    {
+      const int split2 = __ldcg(f.rp.ntiles + 4);
+      const int nj = f.H / 128;
+      for (long u = ew; u < (long)f.T * nj; u += nw) {
+        const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
+        if (f.has_link) {
+          bool valid = false;
+          for (int k = 0; k < f.topk; ++k) valid |= __ldcg(f.inv + t * f.topk + k) >= 0;
+          if (!valid) continue;
+          const int src = t / f.link.cap, j = t - src * f.link.cap;
+          __nv_bfloat16* row = f.link.ret[src] + (size_t)(f.link.rank * f.link.cap + j) * f.H;
+          combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk, 0,
+                       row, j0, lane);
+        } else {
+          combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk,
+                       f.accumulate, f.out + (size_t)t * f.H, j0, lane);
+        }
+      }
+    }
+    // ---- final arrival: the last CTA publishes (NVLink) and zeroes the counter
+    if (f.has_link) __threadfence_system();  // this thread's peer stores first
+    epi_bar_sync(NEPI);
+    if (leader) {
+      if (f.has_link) __threadfence_system();
+      else __threadfence();
+      const unsigned prev = atomicAdd(f.gbar, 1u);
+      if (prev == 5 * G - 1) {
+        if (f.has_link) {
+          __threadfence_system();
+          const long long epoch = *f.link.epoch;
+          for (int r = 0; r < f.link.n_ranks; ++r)
+            st_release_sys(f.link.flag_r[r] + f.link.rank, epoch);
+        }
+        atomicExch(f.gbar, 0u);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
 
 // ---------------------------------------------------------------- small batch
 // (GEMV kernels in moe_gemv.cuh)
@@ -753,6 +956,101 @@ static size_t overlap_workspace(int k, int I) {
   return al(64 * sizeof(unsigned long long)) + al(sizeof(float) * ((size_t)k * I + I + 1));
 }
 
+// The one-launch path is taken with D3_MOE_FUSED=1 (read per call); by
+// default every call takes the separate launches, which measured faster so
+// far (45.3 against 59.5 us at the 8-GPU expert-parallel rank shape).
+static bool fused_enabled() {
+  const char* s = getenv("D3_MOE_FUSED");
+  return s && s[0] == '1';
+}
+
+constexpr int kFusedDeclined = 1;   // not an error: take the separate launches
+
+// Launches moe_fused_kernel for the call planned in pl / rp; returns
+// kFusedDeclined when the shape does not fit it (route scratch beyond the
+// stage ring, or fewer resident CTAs than SMs).
+template <int BN, int KPS>
+static int launch_fused(const Plan& pl, RouteParams rp, char* ws, const void* x,
+                        const void* weights, int weights_f32, int T, int topk, const void* w13,
+                        const float* s13, const void* w2, const float* s2, int n_experts, int H,
+                        int I, void* out, int accumulate, int* err_word, const P2pLink* link,
+                        cudaStream_t st) {
+  using Cfg = GemmCfg<BN, KPS>;
+  const int sms = num_sms();
+  const int P = pl.P;
+  // route scratch in the stage ring: cnt, off, tile prefix [n] + pair map [P]
+  // + one histogram of n per sorting warp (<= the CTA's warps)
+  const size_t ring = (size_t)Cfg::STAGES * Cfg::STAGE_BYTES;
+  const size_t rbase = sizeof(int) * (3 * (size_t)n_experts + (size_t)P);
+  if (rbase + sizeof(int) * (size_t)n_experts > ring) return kFusedDeclined;
+  long nw = (long)(ring - rbase) / (long)(sizeof(int) * (size_t)n_experts);
+  const long warps = Cfg::THREADS / 32;
+  nw = nw > warps ? warps : nw;
+  if (nw > (P + 31) / 32) nw = (P + 31) / 32;
+  if (nw < 1) nw = 1;
+  rp.nw = (int)nw;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return kFusedDeclined;
+  if (!attr_set[dev]) {
+    D3_CUDA_TRY(cudaFuncSetAttribute(moe_fused_kernel<BN, KPS>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM),
+                "fused smem attribute");
+    int per_sm = 0;
+    D3_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_fused_kernel<BN, KPS>,
+                                                              Cfg::THREADS, Cfg::SMEM),
+                "fused occupancy");
+    if (per_sm < 1) return kFusedDeclined;
+    attr_set[dev] = true;
+  }
+  int rc = D3_OK;
+  CUtensorMap tw1, tx1, tw2, tx2;
+  uint8_t* xq = (uint8_t*)(ws + pl.o_xq);
+  uint8_t* hq = (uint8_t*)(ws + pl.o_hq);
+  if ((rc = make_tmap_u8(&tw1, w13, H, (uint64_t)n_experts * 2 * I, H, 128))) return rc;
+  if ((rc = make_tmap_u8(&tx1, xq, 2 * H, pl.Ppad, 2 * H, BN))) return rc;
+  if ((rc = make_tmap_u8(&tw2, w2, I, (uint64_t)n_experts * H, I, 128))) return rc;
+  if ((rc = make_tmap_u8(&tx2, hq, 2 * I, pl.Ppad, 2 * I, BN))) return rc;
+  FusedParams f{};
+  f.rp = rp;
+  f.g1.tiles = rp.tiles1; f.g1.ntiles = rp.ntiles; f.g1.wscale = s13;
+  f.g1.rows_per_expert = 2 * I; f.g1.mblocks = 2 * I / 128; f.g1.kblocks = H / 128;
+  f.g1.xscale = (const float*)(ws + pl.o_xs); f.g1.K = H; f.g1.out = (float*)(ws + pl.o_ws1);
+  f.g1.P = P; f.g1.Mtot = 2 * I; f.g1.err = err_word;
+  f.g2.tiles = rp.tiles2; f.g2.ntiles = rp.ntiles + 1; f.g2.wscale = s2;
+  f.g2.rows_per_expert = H; f.g2.mblocks = H / 128; f.g2.kblocks = I / 128;
+  f.g2.xscale = (const float*)(ws + pl.o_hs); f.g2.K = I; f.g2.out = (float*)(ws + pl.o_ws2);
+  f.g2.P = P; f.g2.Mtot = H; f.g2.err = err_word;
+  f.I = I; f.H = H; f.P = P; f.T = T; f.topk = topk;
+  f.weights_f32 = weights_f32 ? 1 : 0; f.accumulate = accumulate ? 1 : 0;
+  f.ws1 = (const float*)(ws + pl.o_ws1);
+  f.hq = hq;
+  f.hs = (float*)(ws + pl.o_hs);
+  f.ws2 = (const float*)(ws + pl.o_ws2);
+  f.inv = rp.inv;
+  f.weights = weights;
+  f.out = static_cast<__nv_bfloat16*>(out);
+  f.gbar = reinterpret_cast<unsigned*>(ws);
+  f.err = err_word;
+  f.has_link = link ? 1 : 0;
+  if (link) f.link = *link;
+  (void)x;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)sms);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  D3_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_fused_kernel<BN, KPS>, tw1, tx1, tw2, tx2, f),
+              "moe_fused_kernel launch");
+  return D3_OK;
+}
+
 }  // namespace d3
 
 using namespace d3;
@@ -854,6 +1152,15 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   if (link) {
     rp.wait_flags = link->wait_flags; rp.wait_epoch = link->epoch; rp.wait_n = link->n_ranks;
     rp.wait_err = link->err; rp.wait_code = link->wait_code; rp.wait_budget = link->budget_ns;
+  }
+  if (rp.fuse_quant && fused_enabled()) {
+    const int rc = pl.BN == 16 ? launch_fused<16, 2>(pl, rp, ws, x, weights, weights_f32, T, topk,
+                                                     w13, s13, w2, s2, n_experts, H, I, out,
+                                                     accumulate, err_word, link, st)
+                               : launch_fused<64, 2>(pl, rp, ws, x, weights, weights_f32, T, topk,
+                                                     w13, s13, w2, s2, n_experts, H, I, out,
+                                                     accumulate, err_word, link, st);
+    if (rc != kFusedDeclined) return rc;
   }
   const bool pdl = pdl_enabled();
   // shared memory: cnt, off, tile prefix [n] + sorted [P] (fused) + NW chunk
@@ -1019,6 +1326,8 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   gp.sw2 = static_cast<const __nv_bfloat16*>(shared_w2);
   gp.sgate = static_cast<const __nv_bfloat16*>(shared_gate);
   gp.w2_early = 0;
+  gp.fetch_slot = L->fetch_slot;   // the down launch loads every other slot's W2 early
+  gp.nmiss = L->nmiss;
   // stages: 1 allocator, 2 fetch + gate/up, 4 down projection; a call's
   // first launch is an ordinary stream dependent (no programmatic launch)
   if (!(stages & 3)) return run_gemv2(gp, st, false);

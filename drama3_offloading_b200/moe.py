@@ -48,6 +48,7 @@ ERROR_CODES = {
     2: "expert GEMM: the MMA issuer waited for loaded operands or a free accumulator",
     3: "expert GEMM: the final wait for the CTA's own MMAs",
     4: "expert GEMM: the epilogue waited for an accumulator",
+    5: "expert call (one launch): a grid-wide phase barrier or the down-projection operand gate",
     31: "expert parallel: a source rank's dispatch never arrived",
     32: "expert parallel: a serving rank's returned rows never arrived",
     41: "decode overlap: a fetched expert's bytes never landed",

@@ -129,6 +129,7 @@ def test_device_error_codes_are_named():
     text = "".join(f.read_text() for f in sorted(src.glob("*.cu*")))
     codes = {int(c) for c in re.findall(r"gemm_error\(p\.err, (\d+)\)", text)}
     codes |= {int(c) for c in re.findall(r"err_code = (\d+)", text)}
+    codes |= {int(c) for c in re.findall(r"kFusedBarrierCode = (\d+)", text)}
     codes |= {31, 32}   # the expert-parallel waits' codes, passed in by ep.py
     assert codes and codes <= set(moe.ERROR_CODES), codes - set(moe.ERROR_CODES)
     assert moe.error_message(999) == "unknown bounded wait"
