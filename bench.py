@@ -702,6 +702,20 @@ def run_ep(args, rank, world, local):
     eb = synth_expert_bytes(2048, 512)
     per_layer_us, per_layer_bytes = [], []
     reps = 10
+    # with the NVLink exchange the step runs the folded call
+    # (d3_moe_fp8_forward_p2p): time that call, on a local stand-in of the
+    # link (dispatch flags already at the epoch, every source's return rows a
+    # local scratch), so the replays touch no other rank
+    if m.p2p is not None:
+        import ctypes
+        n = world * m.cap
+        lk_flags = torch.ones(world, dtype=torch.int64, device=dev)
+        lk_epoch = torch.ones(1, dtype=torch.int64, device=dev)
+        lk_ret = torch.empty(n, m.H, dtype=torch.bfloat16, device=dev)
+        lk_fr = torch.zeros(world, dtype=torch.int64, device=dev)
+        lk_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+        lk_ret_p = (ctypes.c_void_p * world)(*([lk_ret.data_ptr()] * world))
+        lk_fr_p = (ctypes.c_void_p * world)(*([lk_fr.data_ptr()] * world))
     for l in range(args.layers):
         wl = m.w[l]
         if m.exchange == "none":
@@ -710,9 +724,16 @@ def run_ep(args, rank, world, local):
         else:
             bufs = m.p2p if m.p2p is not None else m
             xin, ids_in, w_in = bufs.recv_x, bufs.recv_eid.view(-1, 1), m.ones
-        fn = lambda: moe.fp8_moe_forward(xin, ids_in, w_in, wl.w13_weight, wl.w13_scale_inv,
-                                         wl.w2_weight, wl.w2_scale_inv, out=m.y if
-                                         m.exchange != "none" else None)
+        if m.p2p is not None:
+            fn = lambda: moe.fp8_moe_forward_p2p(
+                xin, ids_in, w_in, wl.w13_weight, wl.w13_scale_inv, wl.w2_weight,
+                wl.w2_scale_inv, wait_flags=lk_flags, epoch=lk_epoch, n_ranks=world, rank=rank,
+                cap=m.cap, peer_ret=lk_ret_p, peer_flag_r=lk_fr_p, counter=lk_ctr, wait_code=31,
+                budget_ns=m.WAIT_BUDGET_NS)
+        else:
+            fn = lambda: moe.fp8_moe_forward(xin, ids_in, w_in, wl.w13_weight, wl.w13_scale_inv,
+                                             wl.w2_weight, wl.w2_scale_inv, out=m.y if
+                                             m.exchange != "none" else None)
         s_ = torch.cuda.Stream(device=dev)
         s_.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s_):
@@ -770,8 +791,10 @@ def run_ep(args, rank, world, local):
                      "achieved": gemm_gbs, "peak": hbm, "unit": "GB/s", "frac": gemm_gbs / hbm,
                      "traffic": None, "per_rank_gbs": gbs_all,
                      "bytes": "distinct local experts x 3,146,496 B per layer",
-                     "timing": "the rank's expert call replayed from a CUDA graph (10 calls) "
-                               "per layer on its last received rows, CUDA events",
+                     "timing": "the rank's expert call as the step runs it (with the NVLink "
+                               "exchange: the folded call on a local stand-in of the link) "
+                               "replayed from a CUDA graph (10 calls) per layer on its last "
+                               "received rows, CUDA events",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "overflow_pairs": overflow, "clocks": clk.summary(),
         "gpu_launches": args.steps * args.layers * per_layer,

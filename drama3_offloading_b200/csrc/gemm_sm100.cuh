@@ -66,7 +66,11 @@ struct GemmCfg {
   static constexpr int EPI = BN >= 64 ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI;
   static constexpr int CPT = BN * 4 / EPI;
-  static constexpr int SCALE_BYTES = kGemmMaxTileKb * BN * 4;
+  // per-tile promotion scales, double-buffered: a tile's scales are loaded
+  // while the previous tile is promoted
+  static constexpr int SCALE_FLOATS = kGemmMaxTileKb * BN;
+  static constexpr int SCALE_BYTES = 2 * SCALE_FLOATS * 4;
+  static constexpr int SPT = (SCALE_FLOATS + 32 * EPI - 1) / (32 * EPI);  // entries per thread
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + SCALE_BYTES + 256;
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
 };
@@ -88,7 +92,7 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 template <int BN, int KPS>
 struct GemmSmem {
   uint8_t* stage_base;   // [STAGES][STAGE_BYTES]
-  float* s_scale;        // [kGemmMaxTileKb][BN]
+  float* s_scale;        // [2][kGemmMaxTileKb][BN]
   uint64_t* full;        // [STAGES]
   uint64_t* empty;       // [STAGES]
   uint64_t* accf;        // [NB] accumulator ready
@@ -263,29 +267,63 @@ __device__ void gemm_epilogue(const GemmSmem<BN, KPS>& sm, uint32_t tmem, const 
   const int col0 = ((warp - 2) >> 2) * CPT;
   const int row = q * 32 + lane;                 // weight row within the M tile
   const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + col0;
-  float* s_scale = sm.s_scale;
-  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    const int4 tl = __ldcg(p.tiles + t);
+  constexpr int SPT = Cfg::SPT;
+  // Promotion scales of a tile: scale[j][n] = s_w[kb0+j] * s_x[row0+n][kb0+j],
+  // thread ep owns entries ep + k*NEPI.  They are loaded one tile ahead (the
+  // tile descriptors two ahead) into registers, so the loads are long done
+  // when the tile starts and its staging costs no memory round trip.
+  // Coherent (L2) loads, never the non-coherent read-only path: under
+  // programmatic launch this kernel's lifetime overlaps the kernels that
+  // write the activation scales (for a reused workspace, a line cached by an
+  // earlier call could otherwise be served stale).
+  float pw[SPT], px[SPT];
+  auto load_scales = [&](const int4 tl) {
+    const int e = tl.x, m = tl.y & 0xffff, row0 = tl.z;
+    const int ncount = tl.w & 0xFF;
+    const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
+    const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
+#pragma unroll
+    for (int k = 0; k < SPT; ++k) {
+      const int i = ep + k * NEPI;
+      const int j = i / BN, n = i - j * BN;
+      const bool live = j < kb1 - kb0 && n < ncount;
+      pw[k] = live ? __ldcg(ws + kb0 + j) : 0.f;
+      px[k] = live ? __ldcg(p.xscale + (size_t)(row0 + n) * p.kblocks + kb0 + j) : 0.f;
+    }
+  };
+  int t = blockIdx.x;
+  int4 tl_cur = make_int4(0, 0, 0, 0), tl_nxt = make_int4(0, 0, 0, 0);
+  if (t < ntiles) {
+    tl_cur = __ldcg(p.tiles + t);
+    load_scales(tl_cur);
+    if (t + (int)gridDim.x < ntiles) tl_nxt = __ldcg(p.tiles + t + gridDim.x);
+  }
+  int buf = 0;
+  for (; t < ntiles; t += gridDim.x) {
+    const int4 tl = tl_cur;
     const int e = tl.x, m = tl.y & 0xffff, row0 = tl.z;
     const int ncount = tl.w & 0xFF;
     const int kb0 = (tl.w >> 8) & 0xFFF, kb1 = (tl.w >> 20) & 0xFFF;
     const int nkb = kb1 - kb0;
-    // stage this tile's promotion scales: scale[j][n] = s_w[kb0+j] * s_x[row0+n][kb0+j]
-    epi_bar_sync(NEPI);  // every epilogue thread is done with the previous tile's scales
-    if (ep == 0) *s_tile_abort = *s_abort;
-    const float* ws = p.wscale + ((size_t)e * p.mblocks + m) * p.kblocks;
-    // Coherent (L2) loads, never the non-coherent read-only path: under
-    // programmatic launch this kernel's lifetime overlaps the kernels that
-    // write these scales (for a reused workspace, a line cached by an
-    // earlier call could otherwise be served stale).
-    for (int i = ep; i < nkb * BN; i += NEPI) {
-      const int j = i / BN, n = i - j * BN;
-      s_scale[i] = n < ncount
-                       ? __ldcg(ws + kb0 + j) *
-                             __ldcg(p.xscale + (size_t)(row0 + n) * p.kblocks + kb0 + j)
-                       : 0.f;
+    (void)e;
+    // this tile's scales into buffer `buf` (last read two tiles ago: every
+    // thread has passed the previous tile's barrier since)
+    float* s_scale = sm.s_scale + buf * Cfg::SCALE_FLOATS;
+#pragma unroll
+    for (int k = 0; k < SPT; ++k) {
+      const int i = ep + k * NEPI;
+      if (i < Cfg::SCALE_FLOATS) s_scale[i] = pw[k] * px[k];
     }
+    if (ep == 0) *s_tile_abort = *s_abort;
     epi_bar_sync(NEPI);
+    // the next tile's scales and the descriptor after it, in flight while
+    // this tile is promoted
+    const bool has_next = t + (int)gridDim.x < ntiles;
+    int4 tl_after = tl_nxt;
+    if (has_next) {
+      load_scales(tl_nxt);
+      if (t + 2 * (int)gridDim.x < ntiles) tl_after = __ldcg(p.tiles + t + 2 * gridDim.x);
+    }
     // the abort decision is taken once per tile from one shared word, so all
     // epilogue threads leave together (none is left waiting at a barrier)
     if (*s_tile_abort) break;
@@ -338,6 +376,9 @@ __device__ void gemm_epilogue(const GemmSmem<BN, KPS>& sm, uint32_t tmem, const 
       }
       ps.it += g;
     }
+    tl_cur = tl_nxt;
+    tl_nxt = tl_after;
+    buf ^= 1;
     if (!ok) continue;  // leaves at the next tile's shared abort decision
     const int split = tl.y >> 16;  // K-split index of this tile
     float* o = p.out + ((size_t)split * p.P + row0 + col0) * p.Mtot + m * 128 + row;

@@ -199,7 +199,7 @@ __device__ __forceinline__ int pick_split(int tiles, int nkb, int lo, int hi, in
   return (nkb + per - 1) / per;
 }
 
-// Grid of G CTAs x 1024 threads.  Every CTA computes the same stable
+// Grid of G CTAs (512 threads for the route launch).  Every CTA computes the same stable
 // counting sort of the pairs by expert in its own shared memory (no
 // cross-CTA communication; identical inputs give identical results), then
 // the CTAs share the writing: the tile lists (one entry per thread,
@@ -212,7 +212,7 @@ __device__ __forceinline__ int pick_split(int tiles, int nkb, int lo, int hi, in
 // pair at off[e] + base[w][e] + (rank among the equal ids of its 32-pair
 // batch) -- exactly the order of a sequential walk.
 // Dynamic shared memory (ints): cnt[n], off[n], tile prefix[n], hist[NW][n],
-// then the pair -> sorted row map [P] when the quantisation is fused.
+// then the sorted row -> pair map [P] when the quantisation is fused.
 __device__ __forceinline__ int route_chunk(int P, int nw) {
   const int batches = (P + 31) / 32;
   return (batches + nw - 1) / nw * 32;
@@ -226,7 +226,7 @@ __device__ __forceinline__ void route_body(const RouteParams& p, int* sm) {
   int* s_off = sm + n;            // [n]
   int* s_tp = sm + 2 * n;         // [n] exclusive prefix of N tiles per expert
   int* hist = sm + 3 * n;         // [NW][n]
-  int* s_inv = hist + (size_t)NW * n;     // [P] pair -> sorted row (fused quantisation only)
+  int* s_sorted = hist + (size_t)NW * n;  // [P] sorted row -> pair (fused quantisation only)
   __shared__ int warp_tot[32], wt2[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool lead = blockIdx.x == 0;
@@ -241,22 +241,9 @@ __device__ __forceinline__ void route_body(const RouteParams& p, int* sm) {
     __syncthreads();
   }
   for (int i = tid; i < NW * n; i += blockDim.x) hist[i] = 0;
-  // this warp's first sweep of quantisation units (pair, K block), over all
-  // pairs: the activation rows are known by pair index, so their loads are
-  // in flight together with the ids'; rows of skipped pairs are never stored
   const int nkb = p.H / 128;
-  const long long qunits = p.fuse_quant ? (long long)p.P * nkb : 0;
   const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp;
   const int gwarps = gridDim.x * (blockDim.x >> 5);
-  float xv[4][4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const long long u = (long long)gwarp * 4 + q;
-    if (u < qunits) {
-      const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
-      load_x_block(p.x, pair, p.topk, p.H, kb, xv[q]);
-    }
-  }
   __syncthreads();
   const int C = route_chunk(p.P, NW);
   // ---- pass 1: per-chunk counts (leaders of a batch hold distinct ids);
@@ -362,7 +349,7 @@ __device__ __forceinline__ void route_body(const RouteParams& p, int* sm) {
           pos = s_off[e] + base + __popc(m & ((1u << lane) - 1));
           if (lead) p.sorted[pos] = i;
         }
-        if (p.fuse_quant) s_inv[i] = pos;
+        if (p.fuse_quant && pos >= 0) s_sorted[pos] = i;
         if (lead) p.inv[i] = pos;
       }
       __syncwarp();
@@ -374,34 +361,26 @@ __device__ __forceinline__ void route_body(const RouteParams& p, int* sm) {
   __syncthreads();
   const int gthreads = gridDim.x * blockDim.x;
   const int gtid = blockIdx.x * blockDim.x + tid;
-  // ---- the quantisation units: hi/lo planes + scale of each valid pair's
-  // row at its sorted position (the GEMM never reads a row past an
-  // expert's pair count, so skipped pairs get none)
-  for (long long u0 = (long long)gwarp * 4; u0 < qunits; u0 += (long long)gwarps * 4) {
-    const bool first = u0 == (long long)gwarp * 4;
+  // ---- the quantisation units (valid sorted row, K block): hi/lo planes +
+  // scale of each valid pair's token row at its sorted position, four units
+  // per warp in flight (the GEMM never reads a row past an expert's pair
+  // count, so skipped pairs get none)
+  // (32-bit unit arithmetic: fused quantisation runs up to 4096 pairs x 128
+  // K blocks; each unit's row and block are decoded once)
+  const int qunits = p.fuse_quant ? nvalid * nkb : 0;
+  for (int u0 = gwarp * 4; u0 < qunits; u0 += gwarps * 4) {
     float v[4][4];
+    int qrow[4], qkb[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const long long u = u0 + q;
-      if (u < qunits) {
-        const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
-        if (first) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) v[q][c] = xv[q][c];
-        } else {
-          load_x_block(p.x, pair, p.topk, p.H, kb, v[q]);
-        }
-      }
+      const int u = u0 + q;
+      qrow[q] = u / nkb;
+      qkb[q] = u - qrow[q] * nkb;
+      if (u < qunits) load_x_block(p.x, s_sorted[qrow[q]], p.topk, p.H, qkb[q], v[q]);
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const long long u = u0 + q;
-      if (u < qunits) {
-        const int pair = (int)(u / nkb), kb = (int)(u - (long long)pair * nkb);
-        const int row = s_inv[pair];
-        if (row >= 0) store_x_block(v[q], p.H, row, kb, p.xq, p.xs);
-      }
-    }
+    for (int q = 0; q < 4; ++q)
+      if (u0 + q < qunits) store_x_block(v[q], p.H, qrow[q], qkb[q], p.xq, p.xs);
   }
   // ---- tile lists: entry (N tile nt, split s, M tile m) at nt*per + s*mt + m;
   // the K split from the real number of N tiles
@@ -704,42 +683,63 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
     epi_grid_sync(f.gbar, 3 * G, NEPI, leader, f.err);
     gemm_epilogue<BN, KPS>(sm, tmem, f.g2, n2, ps, &s_abort, &s_tile_abort);
     epi_grid_sync(f.gbar, 4 * G, NEPI, leader, f.err);
-    // ---- combine: one warp per (token or received row, 128 output columns)
-    {
-      const int split2 = __ldcg(f.rp.ntiles + 4);
-      const int nj = f.H / 128;
-      for (long u = ew; u < (long)f.T * nj; u += nw) {
+  }
+  // ---- combine, on every warp of the CTA (the producer and MMA lanes are
+  // done: their last operands were consumed before the down tiles drained):
+  // one warp per (token or received row, 128 output columns)
+  __syncthreads();
+  {
+    const int nwc = Cfg::THREADS / 32;
+    const long cw = (long)blockIdx.x * nwc + warp, ncw = (long)G * nwc;
+    const int split2 = __ldcg(f.rp.ntiles + 4);
+    const int nj = f.H / 128;
+    if (f.has_link && f.topk == 1) {
+      // received rows: only the valid ones (sorted rows [0, nvalid)), each
+      // stored into its source rank's return rows
+      const int nvalid = __ldcg(f.rp.ntiles + 2);
+      for (long u = cw; u < (long)nvalid * nj; u += ncw) {
+        const int r = (int)(u / nj), j0 = (int)(u - (long)r * nj) * 128;
+        const int t = __ldcg(f.rp.sorted + r);
+        const int src = t / f.link.cap, j = t - src * f.link.cap;
+        __nv_bfloat16* row = f.link.ret[src] + (size_t)(f.link.rank * f.link.cap + j) * f.H;
+        combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, 1, 0, row, j0,
+                     lane);
+      }
+      __threadfence_system();   // this thread's peer stores before the arrival
+    } else if (f.has_link) {
+      for (long u = cw; u < (long)f.T * nj; u += ncw) {
         const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
-        if (f.has_link) {
-          bool valid = false;
-          for (int k = 0; k < f.topk; ++k) valid |= __ldcg(f.inv + t * f.topk + k) >= 0;
-          if (!valid) continue;
-          const int src = t / f.link.cap, j = t - src * f.link.cap;
-          __nv_bfloat16* row = f.link.ret[src] + (size_t)(f.link.rank * f.link.cap + j) * f.H;
-          combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk, 0,
-                       row, j0, lane);
-        } else {
-          combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk,
-                       f.accumulate, f.out + (size_t)t * f.H, j0, lane);
-        }
+        bool valid = false;
+        for (int k = 0; k < f.topk; ++k) valid |= __ldcg(f.inv + t * f.topk + k) >= 0;
+        if (!valid) continue;
+        const int src = t / f.link.cap, j = t - src * f.link.cap;
+        __nv_bfloat16* row = f.link.ret[src] + (size_t)(f.link.rank * f.link.cap + j) * f.H;
+        combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk, 0,
+                     row, j0, lane);
+      }
+      __threadfence_system();
+    } else {
+      for (long u = cw; u < (long)f.T * nj; u += ncw) {
+        const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
+        combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk,
+                     f.accumulate, f.out + (size_t)t * f.H, j0, lane);
       }
     }
-    // ---- final arrival: the last CTA publishes (NVLink) and zeroes the counter
-    if (f.has_link) __threadfence_system();  // this thread's peer stores first
-    epi_bar_sync(NEPI);
-    if (leader) {
-      if (f.has_link) __threadfence_system();
-      else __threadfence();
-      const unsigned prev = atomicAdd(f.gbar, 1u);
-      if (prev == 5 * G - 1) {
-        if (f.has_link) {
-          __threadfence_system();
-          const long long epoch = *f.link.epoch;
-          for (int r = 0; r < f.link.n_ranks; ++r)
-            st_release_sys(f.link.flag_r[r] + f.link.rank, epoch);
-        }
-        atomicExch(f.gbar, 0u);
+  }
+  // ---- final arrival: the last CTA publishes (NVLink) and zeroes the counter
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (f.has_link) __threadfence_system();
+    else __threadfence();
+    const unsigned prev = atomicAdd(f.gbar, 1u);
+    if (prev == 5 * G - 1) {
+      if (f.has_link) {
+        __threadfence_system();
+        const long long epoch = *f.link.epoch;
+        for (int r = 0; r < f.link.n_ranks; ++r)
+          st_release_sys(f.link.flag_r[r] + f.link.rank, epoch);
       }
+      atomicExch(f.gbar, 0u);
     }
   }
   tc_fence_before();
@@ -1168,7 +1168,11 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
   // the budget holds
   const size_t rbase = sizeof(int) * (3 * (size_t)n_experts + (rp.fuse_quant ? (size_t)P : 0));
   long nw = ((long)kRouteSmemBudget - (long)rbase) / (long)(sizeof(int) * (size_t)n_experts);
-  nw = nw < 1 ? 1 : (nw > 32 ? 32 : nw);
+  // 512 threads per route CTA: with its registers (< 64 per thread) a CTA of
+  // the following GEMM (programmatic launch) fits beside it on the same SM
+  // and runs its prologue while the route finishes
+  constexpr int kRouteThreads = 512;
+  nw = nw < 1 ? 1 : (nw > kRouteThreads / 32 ? kRouteThreads / 32 : nw);
   if (nw > (P + 31) / 32) nw = (P + 31) / 32;
   rp.nw = (int)nw;
   const size_t rsmem = rbase + sizeof(int) * (size_t)nw * n_experts;
@@ -1176,18 +1180,18 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
     D3_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)rsmem),
                 "route smem attribute");
-  // CTAs: enough for one sweep of the quantisation (4 blocks per warp) and
-  // of the tile lists (4 entries per thread)
+  // CTAs: enough for the tile lists (one entry per thread per sweep); with the
+  // quantisation folded in, one per SM (the units are instruction-bound: a
+  // CTA on every SM spreads their issue over the whole GPU, and every CTA's
+  // sort of the pairs is cheap)
   long rgrid = (long)(pl.maxt1 + pl.maxt2 + 4095) / 4096;
-  if (rp.fuse_quant) {
-    const long q = ((long)P * (H / 128) + 127) / 128;
-    if (q > rgrid) rgrid = q;
-  }
+  if (rp.fuse_quant) rgrid = num_sms();
   rgrid = rgrid < 1 ? 1 : (rgrid > num_sms() ? num_sms() : rgrid);
   // The first launch of a call is an ordinary stream dependent: whatever the
   // caller queued before it (copies, foreign kernels) must complete first;
   // only the launches inside this call are chained programmatically.
-  D3_CUDA_TRY(launch_k(route_kernel, dim3((unsigned)rgrid), dim3(1024), rsmem, st, false, rp),
+  D3_CUDA_TRY(launch_k(route_kernel, dim3((unsigned)rgrid), dim3(kRouteThreads), rsmem, st, false,
+                       rp),
               "route_kernel launch");
   int rc = D3_OK;
   if (!rp.fuse_quant) {
