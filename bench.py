@@ -1,7 +1,7 @@
 """Benchmark of the routed-MoE expert-offload hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload decode|fetch|prefill|ep|layer] [--impl ours|reference]
+                    [--workload decode|fetch|prefill|ep|ep-rank|layer] [--impl ours|reference]
 
 Workloads:
 
@@ -20,6 +20,10 @@ Workloads:
   sharded over N GPUs, NCCL all-to-all dispatch/combine.
 * ``layer`` -- configs[0]: one MoE layer over 16 tokens with 256 resident
   experts, the CPU restatement timed beside it.
+* ``ep-rank`` -- configs[4], one rank: the expert call of an N-GPU
+  expert-parallel step (``--ep-ranks N``: 256/N local experts, the rank's
+  received rows) on one GPU, through the folded NVLink call on a local
+  stand-in of the link; the per-rank roofline at every N without N GPUs.
 
 Inputs are far larger than L2 (30 GiB host store, 6.9 GiB dense weights, 8 GiB
 cache).  Multi-GPU runs are replicas (each rank its own store, cache and host
@@ -50,8 +54,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "fetch", "ep", "prefill", "layer"),
+    ap.add_argument("--workload", choices=("decode", "fetch", "ep", "ep-rank", "prefill", "layer"),
                     default="decode")
+    ap.add_argument("--ep-ranks", type=int, default=8,
+                    help="ep-rank workload: the N whose per-rank expert call is emulated")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--global-batch", type=int, default=64, help="ep workload: decode streams")
     ap.add_argument("--layers", type=int, default=40)
@@ -815,6 +821,107 @@ def ep_limiter(layer_us, expert_us, dispatch_us, combine_us) -> str:
             f"({', '.join(f'{k} {v:.1f}' for k, v in parts.items())})")
 
 
+# ---------------------------------------------------------------- ep-rank (configs[4], one rank)
+
+def run_ep_rank(args, rank, world, local):
+    """One rank's expert call at the N-GPU expert-parallel shape, on one GPU:
+    the rank's 256/N local experts per layer and its received rows (N sources
+    x cap = (64/N)*8 rows, one routed pair each, uniform top-8 routing of the
+    64-token batch, the rest -1) -- exactly what the expert call of an N-GPU
+    step sees -- through the folded NVLink call (d3_moe_fp8_forward_p2p) on a
+    local stand-in of the link (dispatch flags already at the epoch, return
+    rows local), replayed from a CUDA graph.  Isolates the per-rank expert
+    GEMMs from the exchange, for the roofline at every N on one GPU."""
+    import ctypes
+    from drama3_offloading_b200 import benchutil, moe, synth
+    from drama3_offloading_b200.ep import synth_expert_bytes
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N = args.ep_ranks
+    epr, T_local = 256 // N, args.global_batch // N
+    cap = T_local * 8
+    rows = N * cap
+    layers = args.layers
+    rng = np.random.default_rng(3)
+    eb = synth_expert_bytes(2048, 512)
+    ws = [synth.make_experts(epr, seed=l, device=dev, chunk=16) for l in range(layers)]
+    x = torch.randn(rows, 2048, device=dev).to(torch.bfloat16)
+    ids_l, nd = [], []
+    for l in range(layers):
+        ids = np.full(rows, -1, np.int32)
+        for s_ in range(N):
+            toks = np.stack([rng.permutation(256)[:8] for _ in range(T_local)])
+            mine = toks[toks // epr == 0] % epr
+            ids[s_ * cap: s_ * cap + len(mine)] = mine
+        ids_l.append(torch.from_numpy(ids).to(dev).view(-1, 1))
+        nd.append(len(np.unique(ids[ids >= 0])))
+    ones = torch.ones(rows, 1, device=dev)
+    ret = torch.zeros(rows, 2048, dtype=torch.bfloat16, device=dev)
+    flag_r = torch.zeros(N, dtype=torch.int64, device=dev)
+    flag_d = torch.ones(N, dtype=torch.int64, device=dev)
+    epoch = torch.ones(1, dtype=torch.int64, device=dev)
+    ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer_ret = (ctypes.c_void_p * N)(*([ret.data_ptr()] * N))
+    peer_fr = (ctypes.c_void_p * N)(*([flag_r.data_ptr()] * N))
+
+    def call(l):
+        w = ws[l]
+        moe.fp8_moe_forward_p2p(x, ids_l[l], ones, w.w13_weight, w.w13_scale_inv, w.w2_weight,
+                                w.w2_scale_inv, wait_flags=flag_d, epoch=epoch, n_ranks=N,
+                                rank=0, cap=cap, peer_ret=peer_ret, peer_flag_r=peer_fr,
+                                counter=ctr, wait_code=31, budget_ns=2_000_000_000)
+
+    def step():
+        for l in range(layers):
+            call(l)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with benchutil.ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("timed")
+        a.record()
+        for _ in range(args.steps):
+            g.replay()
+        b.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+    moe.check_errors(dev)
+    us = a.elapsed_time(b) * 1e3 / (args.steps * layers)
+    byt = float(np.mean(nd)) * eb
+    hbm = measured_peaks()["hbm_gbs"]
+    gbs = byt / (us * 1e-6) / 1e9
+    return {
+        "metric": "per-rank expert call us (folded NVLink call, one rank of the N-GPU "
+                  "expert-parallel step, emulated on one GPU)",
+        "value": us, "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": us * layers / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8 weights x (bf16-class hi/lo fp8 activations)",
+        "data": "synthetic (random-init FP8 experts, uniform-random top-8 routing)",
+        "config": {"workload": "ep-rank", "ranks_emulated": N, "experts_per_rank": epr,
+                   "received_rows": rows, "valid_pairs_per_layer": int(np.mean(
+                       [int((i >= 0).sum()) for i in ids_l])), "layers": layers,
+                   "fused_one_launch": os.environ.get("D3_MOE_FUSED", "0") == "1",
+                   "l2": f"inputs > L2 ({layers * epr * eb / 2**30:.1f} GiB of experts)"},
+        "distinct_experts_per_layer": float(np.mean(nd)),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "traffic": None,
+                     "bytes": "distinct local experts x 3,146,496 B per layer"},
+        "clocks": clk.summary(), "gpu_launches": args.steps * layers * 5,
+    }
+
+
 # ---------------------------------------------------------------- main
 
 def reference_arm(args, rank):
@@ -863,8 +970,9 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.workload in ("ep", "prefill", "layer"):
-        run = {"ep": run_ep, "prefill": run_prefill, "layer": run_layer}[args.workload]
+    if args.workload in ("ep", "ep-rank", "prefill", "layer"):
+        run = {"ep": run_ep, "ep-rank": run_ep_rank, "prefill": run_prefill,
+               "layer": run_layer}[args.workload]
         r = run(args, rank, world, local)
         if rank == 0:
             print(json.dumps(r), flush=True)
