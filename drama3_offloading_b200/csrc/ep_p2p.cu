@@ -68,7 +68,8 @@ struct P2pDispatchParams {
 // unused rows of this source's block on destination d (-1).  The last CTA to
 // finish advances the epoch and publishes it in every destination's flag_d
 // with a system-scope release, after a system fence that orders every CTA's
-// peer stores (each fenced before its arrival) first.
+// peer stores first (each CTA fences once, after its barrier, before its
+// arrival).
 __global__ void __launch_bounds__(128) p2p_dispatch_kernel(P2pDispatchParams p) {
   __shared__ int s_cnt[kP2pMaxRanks];
   __shared__ int s_before;
@@ -115,12 +116,17 @@ __global__ void __launch_bounds__(128) p2p_dispatch_kernel(P2pDispatchParams p) 
   if (i < p.n_ranks)
     for (int j = min(s_cnt[i], p.cap) + tid; j < p.cap; j += blockDim.x)
       p.recv_eid[i][p.rank * p.cap + j] = -1;
-  __threadfence_system();
+  // one system-scope fence per CTA, after the barrier: cumulative over every
+  // peer store this CTA made
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  if (tid == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence_system();
+  if (tid == 0) __threadfence_system();
+  __syncthreads();
   if (tid < p.n_ranks) st_release_sys(p.flag_d[tid] + p.rank, epoch);
   if (tid == 0) { *p.epoch = epoch; *p.counter = 0; }
 }
@@ -147,12 +153,15 @@ __global__ void __launch_bounds__(128) p2p_return_kernel(P2pReturnParams p) {
     uint4* dst = reinterpret_cast<uint4*>(p.ret[s] + (size_t)(p.rank * p.cap + j) * p.H);
     for (int v = threadIdx.x; v < p.H / 8; v += blockDim.x) dst[v] = src[v];
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence_system();
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncthreads();
   if (threadIdx.x < p.n_ranks) st_release_sys(p.flag_r[threadIdx.x] + p.rank, *p.epoch);
   if (threadIdx.x == 0) *p.counter = 0;
 }

@@ -498,38 +498,61 @@ __global__ void combine_kernel(const float* ws2, const int* split_ptr, int P, in
                out + (size_t)t * H, j0, threadIdx.x & 31);
 }
 
-// Expert-parallel NVLink return: one CTA per received row (t = source s *
-// cap + j); the combined row is stored straight into row (rank * cap + j) of
-// source s's return buffer (rows without a valid pair are never read there
-// and are skipped).  The last CTA to finish publishes the epoch in every
-// source's flag_r (system fence first: every CTA fenced its peer stores
-// before its arrival).
+// Expert-parallel NVLink return: warp units (received row t = source s * cap
+// + j, 128 output columns) over a fixed grid; the combined row goes straight
+// into row (rank * cap + j) of source s's return buffer.  With one routed
+// pair per received row (topk == 1, the expert-parallel layout) only the
+// valid rows -- sorted rows [0, nvalid) -- are visited; rows without a valid
+// pair are never read at the source and are skipped.  After its CTA barrier
+// one thread per CTA fences at system scope (cumulative over the CTA's peer
+// stores) and arrives; the last CTA fences once more and releases the epoch
+// in every source's flag_r, one thread per source.
 __global__ void __launch_bounds__(256) combine_return_kernel(const float* ws2,
                                                              const int* split_ptr, int P, int H,
-                                                             const int* inv, const void* weights,
-                                                             int weights_f32, int topk,
+                                                             const int* inv, const int* sorted,
+                                                             const int* nvalid_ptr,
+                                                             const void* weights,
+                                                             int weights_f32, int T, int topk,
                                                              P2pLink link) {
   __shared__ bool s_last;
   pdl_trigger();
   pdl_wait();
-  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  bool valid = false;
-  for (int k = 0; k < topk; ++k) valid |= __ldcg(inv + t * topk + k) >= 0;
-  if (valid) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long gw = (long)blockIdx.x * (blockDim.x >> 5) + warp;
+  const long nw = (long)gridDim.x * (blockDim.x >> 5);
+  const int split = __ldcg(split_ptr);
+  const int nj = H / 128;
+  auto row_of = [&](int t) {
     const int s = t / link.cap, j = t - s * link.cap;
-    __nv_bfloat16* row = link.ret[s] + (size_t)(link.rank * link.cap + j) * H;
-    const int split = *split_ptr;
-    for (int j0 = warp * 128; j0 < H; j0 += (blockDim.x >> 5) * 128)
-      combine_unit(ws2, split, P, H, inv, weights, weights_f32, t, topk, 0, row, j0, lane);
+    return link.ret[s] + (size_t)(link.rank * link.cap + j) * H;
+  };
+  if (topk == 1) {
+    const int nv = __ldcg(nvalid_ptr);
+    for (long u = gw; u < (long)nv * nj; u += nw) {
+      const int r = (int)(u / nj), j0 = (int)(u - (long)r * nj) * 128;
+      const int t = __ldcg(sorted + r);
+      combine_unit(ws2, split, P, H, inv, weights, weights_f32, t, 1, 0, row_of(t), j0, lane);
+    }
+  } else {
+    for (long u = gw; u < (long)T * nj; u += nw) {
+      const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
+      bool valid = false;
+      for (int k = 0; k < topk; ++k) valid |= __ldcg(inv + t * topk + k) >= 0;
+      if (valid)
+        combine_unit(ws2, split, P, H, inv, weights, weights_f32, t, topk, 0, row_of(t), j0,
+                     lane);
+    }
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(link.counter, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(link.counter, 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence_system();
-  const long long epoch = *link.epoch;
-  if (threadIdx.x < link.n_ranks) st_release_sys(link.flag_r[threadIdx.x] + link.rank, epoch);
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < link.n_ranks) st_release_sys(link.flag_r[threadIdx.x] + link.rank, *link.epoch);
   if (threadIdx.x == 0) *link.counter = 0;
 }
 
@@ -705,7 +728,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
         combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, 1, 0, row, j0,
                      lane);
       }
-      __threadfence_system();   // this thread's peer stores before the arrival
     } else if (f.has_link) {
       for (long u = cw; u < (long)f.T * nj; u += ncw) {
         const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
@@ -717,7 +739,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
         combine_unit(f.ws2, split2, f.P, f.H, f.inv, f.weights, f.weights_f32, t, f.topk, 0,
                      row, j0, lane);
       }
-      __threadfence_system();
     } else {
       for (long u = cw; u < (long)f.T * nj; u += ncw) {
         const int t = (int)(u / nj), j0 = (int)(u - (long)t * nj) * 128;
@@ -727,20 +748,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, KPS>::THREADS, 1)
     }
   }
   // ---- final arrival: the last CTA publishes (NVLink) and zeroes the counter
+  // (thread 0's system fence after the CTA barrier covers every peer store
+  // the CTA made)
   __syncthreads();
   if (threadIdx.x == 0) {
     if (f.has_link) __threadfence_system();
     else __threadfence();
-    const unsigned prev = atomicAdd(f.gbar, 1u);
-    if (prev == 5 * G - 1) {
-      if (f.has_link) {
-        __threadfence_system();
-        const long long epoch = *f.link.epoch;
-        for (int r = 0; r < f.link.n_ranks; ++r)
-          st_release_sys(f.link.flag_r[r] + f.link.rank, epoch);
-      }
-      atomicExch(f.gbar, 0u);
-    }
+    s_tile_abort = atomicAdd(f.gbar, 1u) == 5 * G - 1;   // (reused as "last CTA")
+    if (s_tile_abort && f.has_link) __threadfence_system();
+  }
+  __syncthreads();
+  if (s_tile_abort) {
+    if (f.has_link && (int)threadIdx.x < f.link.n_ranks)
+      st_release_sys(f.link.flag_r[threadIdx.x] + f.link.rank, *f.link.epoch);
+    if (threadIdx.x == 0) atomicExch(f.gbar, 0u);
   }
   tc_fence_before();
   __syncthreads();
@@ -1235,9 +1256,13 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
                    : launch_gemm<64, 2>(tw2, tx2, g2, pl.maxt2, st);
   if (rc) return rc;
   if (link) {
-    D3_CUDA_TRY(launch_k(combine_return_kernel, dim3((unsigned)T), dim3(256), 0, st, pdl,
+    // up to one CTA per received row (8 warps each: a row's 128-column
+    // blocks in one sweep); CTAs past the valid rows only arrive
+    const int cgrid = T < 16 * num_sms() ? T : 16 * num_sms();
+    D3_CUDA_TRY(launch_k(combine_return_kernel, dim3((unsigned)cgrid), dim3(256), 0, st, pdl,
                          (const float*)ws2, (const int*)(rp.ntiles + 4), P, H, (const int*)rp.inv,
-                         weights, weights_f32, topk, *link),
+                         (const int*)rp.sorted, (const int*)(rp.ntiles + 2), weights, weights_f32,
+                         T, topk, *link),
                 "combine_return_kernel launch");
   } else {
     const dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)T);
