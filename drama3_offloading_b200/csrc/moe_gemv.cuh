@@ -272,6 +272,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   extern __shared__ __align__(16) float s_h[];   // [topk][I / 16][20]
   __shared__ float s_w[64];
   __shared__ int s_e[64];
+  __shared__ unsigned char s_early[64];
   // the W2 block scales of this CTA's rows (all in one 128-row block) per pair
   __shared__ float s_sc[64][kGemvMaxKbI];
   pdl_trigger();
@@ -285,24 +286,27 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   // flight writes its slot's W2/S2 bytes: its first W2 row and scales are
   // loaded before griddepcontrol.wait, so they stream in while the gate/up
   // products finish.
-  int my_e = -1;
-  bool my_early = false;
-  if (lane < topk) {
-    my_e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + lane, p.n);
-    my_early = p.w2_early != 0;
-    if (!my_early && my_e >= 0 && p.fetch_slot) {
+  // Every pair's expert and early flag, once per CTA into shared memory
+  // before the wait (the scale staging and the sums below read them there,
+  // so nothing after the wait repeats the ids or the job table).
+  if (threadIdx.x < topk) {
+    const int e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + threadIdx.x, p.n);
+    bool ea = p.w2_early != 0;
+    if (!ea && e >= 0 && p.fetch_slot) {
       const int nm = __ldcg(p.nmiss);
       bool fetched = false;
-      for (int jj = 0; jj < nm; ++jj) fetched |= __ldcg(p.fetch_slot + jj) == my_e;
-      my_early = !fetched;
+      for (int jj = 0; jj < nm; ++jj) fetched |= __ldcg(p.fetch_slot + jj) == e;
+      ea = !fetched;
     }
+    s_e[threadIdx.x] = e;
+    s_early[threadIdx.x] = ea ? 1 : 0;
   }
-  const unsigned early = __ballot_sync(0xffffffffu, my_early);
+  __syncthreads();
   uint4 w0[kGemvPairGroup][CPL];
 #pragma unroll
   for (int q = 0; q < kGemvPairGroup; ++q) {
-    const int e = __shfl_sync(0xffffffffu, my_e, q);
-    if (((early >> q) & 1u) && q < topk && e >= 0 && j_first < H) {
+    const int e = q < topk ? s_e[q] : -1;
+    if (q < topk && s_early[q] && e >= 0 && j_first < H) {
       const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
@@ -314,16 +318,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   auto stage_scales = [&](bool want_early) {
     for (int i = threadIdx.x; i < topk * nkbI; i += blockDim.x) {
       const int k = i / nkbI, kb = i - k * nkbI;
-      const int e = gemv_pair_id(p.ids, p.ids_bytes, t * topk + k, p.n);
+      const int e = s_e[k];
       if (e < 0) continue;
-      bool is_early = p.w2_early != 0;
-      if (!is_early && p.fetch_slot) {
-        const int nm = __ldcg(p.nmiss);
-        bool fetched = false;
-        for (int jj = 0; jj < nm; ++jj) fetched |= __ldcg(p.fetch_slot + jj) == e;
-        is_early = !fetched;
-      }
-      if (is_early == want_early)
+      if ((s_early[k] != 0) == want_early)
         s_sc[k][kb] = __ldcg(p.s2 + ((size_t)e * (H / 128) + rb) * nkbI + kb);
     }
   };
@@ -348,8 +345,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   // wrote), issued before the h staging so both latencies overlap
 #pragma unroll
   for (int q = 0; q < kGemvPairGroup; ++q) {
-    const int e = __shfl_sync(0xffffffffu, my_e, q);
-    if (!((early >> q) & 1u) && q < topk && e >= 0 && j_first < H) {
+    const int e = q < topk ? s_e[q] : -1;
+    if (q < topk && !s_early[q] && e >= 0 && j_first < H) {
       const uint4* wr = reinterpret_cast<const uint4*>(p.w2 + ((size_t)e * H + j_first) * I);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) w0[q][c] = __ldcg(wr + lane + 32 * c);
@@ -368,7 +365,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   const float sgate = (p.sw13 && p.sgate) ? __ldcg(p.gs + t) : 1.f;
   if (threadIdx.x < topk) {
     const int i = t * topk + threadIdx.x;
-    s_e[threadIdx.x] = gemv_pair_id(p.ids, p.ids_bytes, i, p.n);
     s_w[threadIdx.x] = p.weights_f32 ? static_cast<const float*>(p.weights)[i]
                                      : __bfloat162float(
                                            static_cast<const __nv_bfloat16*>(p.weights)[i]);

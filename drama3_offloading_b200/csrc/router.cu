@@ -191,10 +191,6 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
   float* s_logits = reinterpret_cast<float*>(smem_raw);  // [T][E], used in the leader
   double* xd = reinterpret_cast<double*>(smem_raw + router_cluster_logit_bytes(p.E));
   cluster_arrive_relaxed();  // "this CTA has started" (phase 1)
-  // programmatic launch: the next launch may start its prologue now; nothing
-  // of global memory is read before the preceding grid has completed
-  pdl_trigger();
-  pdl_wait();
   const unsigned rank = cluster_ctarank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = p.T;        // <= kRouterClusterMaxT
@@ -202,6 +198,10 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
   const int epc = (p.E + kRouterClusterCtas - 1) / kRouterClusterCtas;
   const int ebase = (int)rank * epc, eend = min(p.E, ebase + epc);
   const int vec = p.H / 8;   // 8-element chunks per row
+  // programmatic launch: the next launch may start its prologue now; nothing
+  // of global memory is read before the preceding grid has completed
+  pdl_trigger();
+  pdl_wait();
   // this warp's first gate row is in flight before the token rows are staged
   const int e0 = ebase + warp;
   uint4 w[8];
@@ -213,10 +213,26 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
       w[u] = c < vec ? __ldg(r + c) : make_uint4(0, 0, 0, 0);
     }
   }
-  const uint16_t* xb = reinterpret_cast<const uint16_t*>(p.x);
-  for (int i = threadIdx.x; i < nt * p.H; i += blockDim.x) {
-    const int t = i / p.H, k = i - t * p.H;
-    xd[((size_t)t * vec + (k >> 3)) * kRouterXChunk + (k & 7)] = bf16_bits_to_f64(xb[i]);
+  // the token rows, staged as fp64: one 16-B load of 8 values per thread
+  // (every load in flight at once), or element loads for an unaligned row
+  if ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) {
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+    for (int c = threadIdx.x; c < nt * vec; c += blockDim.x) {
+      const uint4 q = xv[c];
+      const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+      double* dst = xd + (size_t)c * kRouterXChunk;   // chunk c of token c / vec
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dst[2 * j] = bf16_bits_to_f64(qq[j] & 0xffffu);
+        dst[2 * j + 1] = bf16_bits_to_f64(qq[j] >> 16);
+      }
+    }
+  } else {
+    const uint16_t* xb = reinterpret_cast<const uint16_t*>(p.x);
+    for (int i = threadIdx.x; i < nt * p.H; i += blockDim.x) {
+      const int t = i / p.H, k = i - t * p.H;
+      xd[((size_t)t * vec + (k >> 3)) * kRouterXChunk + (k & 7)] = bf16_bits_to_f64(xb[i]);
+    }
   }
   __syncthreads();
   cluster_wait();  // every CTA of the cluster runs: its shared memory may be written
