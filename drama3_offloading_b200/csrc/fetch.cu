@@ -151,6 +151,7 @@ struct ResolveParams {
   int64_t expert_bytes;
   int64_t* zero;       // [nzero] cleared by this launch (the overlap launch's counters)
   int32_t nzero;
+  int32_t slot_of_smem;  // stage the whole slot_of table in shared memory (1) or look it up (0)
 };
 
 __device__ __forceinline__ int32_t load_id(const void* ids, int bytes, int i) {
@@ -181,8 +182,11 @@ __device__ __forceinline__ void warp_argmin(int64_t& key, int& idx) {
 // that expert; an id seen earlier in the same call resolves to the slot its
 // latest occurrence got (again iff still owned) -- together exactly the
 // reference's live slot_of lookup.
+// Every prefetch load is issued before any is used (batched into registers),
+// so the prefetch is one memory round trip: with slot_of_smem the whole
+// slot_of table is staged alongside the ids instead of looked up by them.
 // Dynamic shared memory: stamp[C] (+ freq[C], ins[C] for LFU) int64, then
-// owner[C] int32.
+// owner[C] int32, then (slot_of_smem) slot_of[num_experts] int32.
 __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   extern __shared__ int64_t sh[];
   const int C = p.capacity;
@@ -191,28 +195,61 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   int64_t* s_freq = sh + C;
   int64_t* s_ins = sh + 2 * C;
   int32_t* s_owner = reinterpret_cast<int32_t*>(sh + (lfu ? 3 : 1) * C);
+  int32_t* s_slot_of = s_owner + C;
   const int lane = threadIdx.x;
   const unsigned full = 0xffffffffu;
+  const int n = p.num_experts;
   pdl_trigger();  // the dependent fetch grid may start launching now
   pdl_wait();     // ids may come from the launch just before this one
-  // ---- parallel prefetch
+  // ---- parallel prefetch: the ids, the slot tables, the step
   int e_lo = -1, e_hi = -1, pre_lo = -1, pre_hi = -1;
-  if (lane < p.k) {
-    e_lo = load_id(p.ids, p.ids_bytes, lane);
-    if (e_lo >= p.num_experts) e_lo = -1;
-    if (e_lo >= 0) pre_lo = p.slot_of[e_lo];
+  if (lane < p.k) e_lo = load_id(p.ids, p.ids_bytes, lane);
+  if (lane + 32 < p.k) e_hi = load_id(p.ids, p.ids_bytes, lane + 32);
+  const int64_t step = *p.step + 1;
+  constexpr int kB = 8;  // loads per lane in flight per batch
+  if (p.slot_of_smem) {
+    for (int base = 0; base < n; base += 32 * kB) {
+      int32_t v[kB];
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        const int i = base + 32 * u + lane;
+        v[u] = i < n ? p.slot_of[i] : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        const int i = base + 32 * u + lane;
+        if (i < n) s_slot_of[i] = v[u];
+      }
+    }
   }
-  if (lane + 32 < p.k) {
-    e_hi = load_id(p.ids, p.ids_bytes, lane + 32);
-    if (e_hi >= p.num_experts) e_hi = -1;
+  for (int base = 0; base < C; base += 32 * kB) {
+    int64_t st[kB];
+    int32_t ow[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int c = base + 32 * u + lane;
+      st[u] = c < C ? p.stamp[c] : 0;
+      ow[u] = c < C ? p.slot_expert[c] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int c = base + 32 * u + lane;
+      if (c < C) { s_stamp[c] = st[u]; s_owner[c] = ow[u]; }
+    }
+  }
+  if (lfu)
+    for (int c = lane; c < C; c += 32) { s_freq[c] = p.freq[c]; s_ins[c] = p.ins[c]; }
+  if (e_lo >= n) e_lo = -1;
+  if (e_hi >= n) e_hi = -1;
+  if (!p.slot_of_smem) {
+    if (e_lo >= 0) pre_lo = p.slot_of[e_lo];
     if (e_hi >= 0) pre_hi = p.slot_of[e_hi];
   }
-  for (int c = lane; c < C; c += 32) {
-    s_stamp[c] = p.stamp[c];
-    s_owner[c] = p.slot_expert[c];
-    if (lfu) { s_freq[c] = p.freq[c]; s_ins[c] = p.ins[c]; }
+  __syncwarp();  // the staged tables are visible to every lane
+  if (p.slot_of_smem) {
+    if (e_lo >= 0) pre_lo = s_slot_of[e_lo];
+    if (e_hi >= 0) pre_hi = s_slot_of[e_hi];
   }
-  const int64_t step = *p.step + 1;
   for (int i = lane; i < p.nzero; i += 32) p.zero[i] = 0;
   __syncwarp();
   int out_lo = -1, out_hi = -1;
@@ -440,9 +477,13 @@ __global__ void lookup_kernel(const int32_t* __restrict__ slot_of, int32_t E, co
 
 // ---------------------------------------------------------------- host side
 
-static int launch_resolve(const ResolveParams& p, cudaStream_t st) {
-  const size_t smem = (size_t)p.capacity * sizeof(int64_t) * (p.policy == D3_POLICY_LFU ? 3 : 1) +
-                      (size_t)p.capacity * sizeof(int32_t);
+static int launch_resolve(ResolveParams p, cudaStream_t st) {
+  size_t smem = (size_t)p.capacity * sizeof(int64_t) * (p.policy == D3_POLICY_LFU ? 3 : 1) +
+                (size_t)p.capacity * sizeof(int32_t);
+  // the whole slot_of table beside the slot tables while that stays small
+  const size_t slot_of_bytes = (size_t)p.num_experts * sizeof(int32_t);
+  p.slot_of_smem = smem + slot_of_bytes <= 64 * 1024 ? 1 : 0;
+  if (p.slot_of_smem) smem += slot_of_bytes;
   if (smem > 48 * 1024) {
     D3_CUDA_TRY(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),

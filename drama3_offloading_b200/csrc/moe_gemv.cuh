@@ -300,6 +300,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
     }
     s_e[threadIdx.x] = e;
     s_early[threadIdx.x] = ea ? 1 : 0;
+    // the combine weights come from the router, which completed before the
+    // allocator did, like the ids
+    const int i = t * topk + threadIdx.x;
+    s_w[threadIdx.x] = p.weights_f32 ? static_cast<const float*>(p.weights)[i]
+                                     : __bfloat162float(
+                                           static_cast<const __nv_bfloat16*>(p.weights)[i]);
   }
   __syncthreads();
   uint4 w0[kGemvPairGroup][CPL];
@@ -355,20 +361,32 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   stage_scales(false);
   // stage the token's pair rows of h (written by the gate/up launch), and the
   // shared expert's row as row topk
+  // (kHB loads per thread issued before the first store: one round trip for
+  // a decode token's 8 pair rows + the shared expert's row)
   const int nrows = topk + (p.sw13 ? 1 : 0);
-  for (int i = threadIdx.x; i < nrows * (I / 4); i += blockDim.x) {
-    const int k = i / (I / 4), f4 = i - k * (I / 4);
-    const float* src = k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I;
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + f4);
-    *reinterpret_cast<float4*>(s_h + k * row_stride + (f4 >> 2) * 20 + (f4 & 3) * 4) = v;
+  const int n4 = nrows * (I / 4);
+  constexpr int kHB = CPL == 1 ? 8 : 4;
+  for (int base = 0; base < n4; base += kHB * kGemvThreads) {
+    float4 hv4[kHB];
+#pragma unroll
+    for (int u = 0; u < kHB; ++u) {
+      const int i = base + u * kGemvThreads + (int)threadIdx.x;
+      if (i < n4) {
+        const int k = i / (I / 4), f4 = i - k * (I / 4);
+        const float* src = k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I;
+        hv4[u] = __ldcg(reinterpret_cast<const float4*>(src) + f4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kHB; ++u) {
+      const int i = base + u * kGemvThreads + (int)threadIdx.x;
+      if (i < n4) {
+        const int k = i / (I / 4), f4 = i - k * (I / 4);
+        *reinterpret_cast<float4*>(s_h + k * row_stride + (f4 >> 2) * 20 + (f4 & 3) * 4) = hv4[u];
+      }
+    }
   }
   const float sgate = (p.sw13 && p.sgate) ? __ldcg(p.gs + t) : 1.f;
-  if (threadIdx.x < topk) {
-    const int i = t * topk + threadIdx.x;
-    s_w[threadIdx.x] = p.weights_f32 ? static_cast<const float*>(p.weights)[i]
-                                     : __bfloat162float(
-                                           static_cast<const __nv_bfloat16*>(p.weights)[i]);
-  }
   __syncthreads();
   // acc += w[t,k] * s2 * (W2[e_k][j] . h_k) over one group of pairs, k in order
   auto group = [&](const uint4 (&w)[kGemvPairGroup][CPL], int k0, float acc) {

@@ -78,10 +78,13 @@ __device__ __forceinline__ float topk_key_value(unsigned key) {
 // Top-k of token t's logits, held by one warp 32-strided (v[j] = logit
 // j*32 + lane, -inf past E; per = ceil(E/32)): fp32 softmax (max, then the
 // per-lane sums in j order combined by a butterfly), k rounds of one warp
-// max-reduction over the selection keys, then the optional renormalisation.
+// max-reduction over the selection keys (a tree over the lane's KPER keys,
+// then one redux; lane r keeps round r's winner), then the k probabilities
+// in parallel, their sum in round order and the optional renormalisation.
 template <int KPER>
 __device__ __forceinline__ void topk_select(const float (&v)[KPER], int per, int t,
                                             const RouterParams& p) {
+  static_assert((KPER & (KPER - 1)) == 0, "KPER must be a power of two");
   const int lane = threadIdx.x & 31;
   float mx = -INFINITY;
 #pragma unroll
@@ -99,20 +102,29 @@ __device__ __forceinline__ void topk_select(const float (&v)[KPER], int per, int
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) denom += __shfl_xor_sync(0xffffffffu, denom, off);
-  float sel_w = 0.f, sel_sum = 0.f;
-  int sel_id = -1;
+  unsigned my_win = 0u;
   for (int r = 0; r < p.topk; ++r) {
-    unsigned best = 0u;
+    unsigned m[KPER];
 #pragma unroll
-    for (int j = 0; j < KPER; ++j) best = max(best, key[j]);
-    const unsigned win = __reduce_max_sync(0xffffffffu, best);
-    const float pr = expf(topk_key_value(win) - mx) / denom;
-    if (lane == r) { sel_id = 0xffff - (int)(win & 0xffffu); sel_w = pr; }
-    sel_sum += pr;
+    for (int j = 0; j < KPER; ++j) m[j] = key[j];
+#pragma unroll
+    for (int w = KPER / 2; w >= 1; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) m[j] = max(m[j], m[j + w]);
+    const unsigned win = __reduce_max_sync(0xffffffffu, m[0]);
+    if (lane == r) my_win = win;
 #pragma unroll
     for (int j = 0; j < KPER; ++j)
       if (key[j] == win) key[j] = 0u;
   }
+  int sel_id = -1;
+  float sel_w = 0.f;
+  if (lane < p.topk) {
+    sel_id = 0xffff - (int)(my_win & 0xffffu);
+    sel_w = expf(topk_key_value(my_win) - mx) / denom;
+  }
+  float sel_sum = 0.f;
+  for (int r = 0; r < p.topk; ++r) sel_sum += __shfl_sync(0xffffffffu, sel_w, r);
   if (lane < p.topk) {
     const float wgt = p.renorm ? sel_w / sel_sum : sel_w;
     p.ids_out[(size_t)t * p.topk + lane] = sel_id;
