@@ -200,6 +200,23 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   const unsigned full = 0xffffffffu;
   const int n = p.num_experts;
   pdl_trigger();  // the dependent fetch grid may start launching now
+  // L2 prefetch hints for every line the prefetch below reads, issued while
+  // the preceding launch (the router) still runs: a hint returns no data and
+  // L2 is the point of coherence, so the loads after the wait still see that
+  // launch's writes; what it saves is the DRAM and address-translation
+  // latency of tables the layers in between have evicted.
+  {
+    auto hint = [&](const void* base, size_t bytes) {
+      for (size_t o = (size_t)lane * 128; o < bytes; o += 32 * 128)
+        prefetch_l2(static_cast<const char*>(base) + o);
+    };
+    hint(p.ids, (size_t)p.k * p.ids_bytes);
+    hint(p.slot_of, (size_t)n * sizeof(int32_t));
+    hint(p.stamp, (size_t)C * sizeof(int64_t));
+    hint(p.slot_expert, (size_t)C * sizeof(int32_t));
+    hint(p.step, sizeof(int64_t));
+    if (lfu) { hint(p.freq, (size_t)C * sizeof(int64_t)); hint(p.ins, (size_t)C * sizeof(int64_t)); }
+  }
   pdl_wait();     // ids may come from the launch just before this one
   // ---- parallel prefetch: the ids, the slot tables, the step
   int e_lo = -1, e_hi = -1, pre_lo = -1, pre_hi = -1;

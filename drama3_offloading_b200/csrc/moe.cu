@@ -1140,13 +1140,13 @@ static int moe_forward(const void* x, const void* ids, int32_t ids_bytes, const 
     gp.accumulate = accumulate ? 1 : 0;
     gp.w13 = static_cast<const uint8_t*>(w13); gp.s13 = s13;
     gp.w2 = static_cast<const uint8_t*>(w2); gp.s2 = s2;
-    gp.h = (float*)(ws + pl.o_ws1);
+    gp.h = (__nv_bfloat16*)(ws + pl.o_ws1);
     gp.out = static_cast<__nv_bfloat16*>(out);
     gp.sw13 = static_cast<const __nv_bfloat16*>(sw13);
     gp.sw2 = static_cast<const __nv_bfloat16*>(sw2);
     gp.sgate = static_cast<const __nv_bfloat16*>(sgate);
     gp.hs = gp.h + (size_t)P * I;
-    gp.gs = gp.hs + (size_t)T * I;
+    gp.gs = reinterpret_cast<float*>(gp.hs + (size_t)T * I);
     gp.w2_early = 1;
     return run_gemv(gp, st);
   }
@@ -1347,9 +1347,9 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   gp.w2 = static_cast<const uint8_t*>(L->cache[1]);
   gp.s13 = static_cast<const float*>(L->cache[2]);
   gp.s2 = static_cast<const float*>(L->cache[3]);
-  gp.h = reinterpret_cast<float*>(ws + al(64 * sizeof(unsigned long long)));
+  gp.h = reinterpret_cast<__nv_bfloat16*>(ws + al(64 * sizeof(unsigned long long)));
   gp.hs = gp.h + (size_t)k * I;
-  gp.gs = gp.hs + I;
+  gp.gs = reinterpret_cast<float*>(gp.hs + I);
   gp.out = static_cast<__nv_bfloat16*>(out);
   gp.sw13 = static_cast<const __nv_bfloat16*>(shared_w13);
   gp.sw2 = static_cast<const __nv_bfloat16*>(shared_w2);

@@ -11,7 +11,9 @@
 //   gemv13   one warp per (pair, intermediate row j): the gate row j and the
 //            up row I + j of the pair's expert against the token row (held in
 //            registers as fp32), per-128 K-block scales applied to the fp32
-//            partial sums, then h[pair, j] = silu(g) * u  (fp32, workspace).
+//            partial sums, then h[pair, j] = silu(g) * u  (workspace, rounded
+//            to bf16 -- the precision the reference's bf16 path holds it in --
+//            which halves the bytes every gemv2 CTA stages).
 //   gemv2    one CTA per (token, 8 output rows): the token's pair rows of h
 //            staged in shared memory; one warp per output row j sums
 //            w[t,k] * s2 * (W2[e_k][j, :] . h[pair_k]) over the token's pairs
@@ -26,8 +28,9 @@
 // sigmoid(x . g) * (W2s[j] . hs[t]) to the same output in the same warp, so
 // the whole MoE block is the same two launches.
 //
-// Activations stay fp32/bf16 (no activation quantisation), so this path is
-// at least as accurate as the tensor-core path; both sum the same products.
+// Activations stay bf16 (no activation quantisation): the token row as given,
+// h rounded once to bf16 (~8 significant bits, as the tensor-core path's
+// hi/lo e4m3 planes carry); the products are summed in fp32.
 // Ids outside [0, n) skip their pair, as everywhere in this library.
 #pragma once
 
@@ -54,14 +57,14 @@ struct GemvParams {
   const float* s13;         // [n, 2I/128, H/128]
   const uint8_t* w2;        // [n, H, I] e4m3
   const float* s2;          // [n, H/128, I/128]
-  float* h;                 // [T*topk, I] workspace
+  __nv_bfloat16* h;         // [T*topk, I] workspace (bf16, as the reference's bf16 path)
   __nv_bfloat16* out;       // [T, H]
   // optional shared expert (every token, bf16, intermediate I): null sw13 =
   // none; null sgate = ungated
   const __nv_bfloat16* sw13;   // [2I, H] (gate rows [0, I), up rows [I, 2I))
   const __nv_bfloat16* sw2;    // [H, I]
   const __nv_bfloat16* sgate;  // [H]
-  float* hs;                   // [T, I] workspace
+  __nv_bfloat16* hs;           // [T, I] workspace
   float* gs;                   // [T] workspace: sigmoid(x . sgate)
   // gemv2 loads its first W2 rows before griddepcontrol.wait (1), or only
   // after it (0: the preceding launch may still be writing W2, as the fetch +
@@ -194,7 +197,7 @@ __device__ __forceinline__ void gemv13_units(const GemvParams& p, long gw, long 
           au += dot16_bf16(__ldcg(ru + 2 * q), __ldcg(ru + 2 * q + 1), xv[c]);
         }
         au = warp_sum(au);
-        if (lane == 0) p.hs[(size_t)t * I + j] = ag / (1.f + expf(-ag)) * au;
+        if (lane == 0) p.hs[(size_t)t * I + j] = __float2bfloat16_rn(ag / (1.f + expf(-ag)) * au);
         continue;
       }
       const int pair = (int)(u / I), j = (int)(u - (long)pair * I);
@@ -247,7 +250,7 @@ __device__ __forceinline__ void gemv13_units(const GemvParams& p, long gw, long 
       }
       ag = warp_sum(ag);
       au = warp_sum(au);
-      if (lane == 0) p.h[u] = ag / (1.f + expf(-ag)) * au;
+      if (lane == 0) p.h[u] = __float2bfloat16_rn(ag / (1.f + expf(-ag)) * au);
     }
   }
 }
@@ -346,6 +349,30 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
       sw0[c][1] = __ldcg(wr + 2 * (lane + 32 * c) + 1);
     }
   }
+  // L2 prefetch hints for what is read right after the wait -- this token's
+  // h rows (and the shared expert's), and the first W2 row of every pair
+  // whose slot the preceding launch fills.  A hint returns no data and L2 is
+  // the point of coherence, so the loads after the wait still see that
+  // launch's writes; the hints only take the DRAM and address-translation
+  // latency out of the tail of the layer.
+  {
+    const int nrows = topk + (p.sw13 ? 1 : 0);
+    const int hl = I * (int)sizeof(*p.h) / 128;   // 128-B lines per h row
+    for (int i = threadIdx.x; i < nrows * hl; i += blockDim.x) {
+      const int k = i / hl, l = i - k * hl;
+      const char* src = reinterpret_cast<const char*>(
+          k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I);
+      prefetch_l2(src + (size_t)l * 128);
+    }
+    if (j_first < H) {   // this warp's output row, for every fetched pair
+      const int wl = I / 128;
+      for (int i = lane; i < topk * wl; i += 32) {
+        const int k = i / wl, l = i - k * wl;
+        if (!s_early[k] && s_e[k] >= 0)
+          prefetch_l2(p.w2 + ((size_t)s_e[k] * H + j_first) * I + (size_t)l * 128);
+      }
+    }
+  }
   pdl_wait();
   // the first group's remaining W2 rows and scales (slots the preceding launch
   // wrote), issued before the h staging so both latencies overlap
@@ -364,25 +391,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) moe_gemv2_kernel(GemvParams p
   // (kHB loads per thread issued before the first store: one round trip for
   // a decode token's 8 pair rows + the shared expert's row)
   const int nrows = topk + (p.sw13 ? 1 : 0);
-  const int n4 = nrows * (I / 4);
+  const int n8 = nrows * (I / 8);   // 16-byte groups of 8 bf16
   constexpr int kHB = CPL == 1 ? 8 : 4;
-  for (int base = 0; base < n4; base += kHB * kGemvThreads) {
-    float4 hv4[kHB];
+  for (int base = 0; base < n8; base += kHB * kGemvThreads) {
+    uint4 hv8[kHB];
 #pragma unroll
     for (int u = 0; u < kHB; ++u) {
       const int i = base + u * kGemvThreads + (int)threadIdx.x;
-      if (i < n4) {
-        const int k = i / (I / 4), f4 = i - k * (I / 4);
-        const float* src = k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I;
-        hv4[u] = __ldcg(reinterpret_cast<const float4*>(src) + f4);
+      if (i < n8) {
+        const int k = i / (I / 8), g8 = i - k * (I / 8);
+        const __nv_bfloat16* src = k < topk ? p.h + (size_t)(t * topk + k) * I : p.hs + (size_t)t * I;
+        hv8[u] = __ldcg(reinterpret_cast<const uint4*>(src) + g8);
       }
     }
 #pragma unroll
     for (int u = 0; u < kHB; ++u) {
       const int i = base + u * kGemvThreads + (int)threadIdx.x;
-      if (i < n4) {
-        const int k = i / (I / 4), f4 = i - k * (I / 4);
-        *reinterpret_cast<float4*>(s_h + k * row_stride + (f4 >> 2) * 20 + (f4 & 3) * 4) = hv4[u];
+      if (i < n8) {
+        const int k = i / (I / 8), g8 = i - k * (I / 8);
+        const uint32_t w4[4] = {hv8[u].x, hv8[u].y, hv8[u].z, hv8[u].w};
+        float f[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          f[2 * q] = __uint_as_float(w4[q] << 16);
+          f[2 * q + 1] = __uint_as_float(w4[q] & 0xffff0000u);
+        }
+        float* dst = s_h + k * row_stride + (g8 >> 1) * 20 + (g8 & 1) * 8;
+        *reinterpret_cast<float4*>(dst) = make_float4(f[0], f[1], f[2], f[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
       }
     }
   }
