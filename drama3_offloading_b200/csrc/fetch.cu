@@ -268,6 +268,13 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
     if (e_hi >= 0) pre_hi = s_slot_of[e_hi];
   }
   for (int i = lane; i < p.nzero; i += 32) p.zero[i] = 0;
+  // LRU victim search on 32-bit keys (two warp reductions) while every stamp
+  // -- and the step the call writes -- fits in int32, which holds for the
+  // first 2^31 calls of a layer; otherwise the 64-bit search
+  bool fits = step <= (int64_t)INT32_MAX;
+  for (int c = lane; c < C; c += 32)
+    fits &= s_stamp[c] >= (int64_t)INT32_MIN && s_stamp[c] <= (int64_t)INT32_MAX;
+  const bool key32 = __all_sync(full, fits);
   __syncwarp();
   int out_lo = -1, out_hi = -1;
   int nmiss = 0, hits = 0;
@@ -290,7 +297,17 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
     }
     if (s < 0) {
       int best = 0x7fffffff;
-      if (!lfu) {
+      if (!lfu && key32) {
+        // lexicographic (stamp, slot) minimum: the lane's own slots in
+        // ascending order, then the minimum stamp and the lowest slot with it
+        int key = INT32_MAX, bi = INT32_MAX;
+        for (int c = lane; c < C; c += 32) {
+          const int v = (int)s_stamp[c];
+          if (v < key) { key = v; bi = c; }
+        }
+        const int m = __reduce_min_sync(full, key);
+        best = __reduce_min_sync(full, key == m ? bi : INT32_MAX);
+      } else if (!lfu) {
         int64_t key = INT64_MAX;
         for (int c = lane; c < C; c += 32)
           if (s_stamp[c] < key) { key = s_stamp[c]; best = c; }

@@ -66,6 +66,42 @@ def test_resolve_slots_matches_reference(golden, case, id_dtype):
     np.testing.assert_array_equal(tabs["step"].cpu().numpy(), g("final_step"))
 
 
+@pytest.mark.parametrize("offset", [2**31 - 24, 2**40])
+def test_resolve_slots_large_stamps(golden, offset):
+    """Stamps and steps past the int32 range take the allocator's 64-bit
+    victim search: starting 24 calls below 2^31 the first calls run the
+    32-bit search and the later ones cross over mid-sequence; starting at
+    2^40 every call runs the 64-bit one.  Slots, jobs and final tables must
+    equal the oracle's, as at small stamps."""
+    g = lambda k: golden[f"zipf_c68/{k}"]
+    E, C = int(g("E")), int(g("C"))
+    ids_all = torch.from_numpy(g("ids")).to(torch.int32).to(DEV)
+    K = ids_all.shape[1]
+    tab = oracle.init_tables(E, C)
+    tab.stamp += offset
+    tab.step += offset
+    tabs = {"slot_of": torch.from_numpy(tab.slot_of.copy()).to(DEV),
+            "slot_expert": torch.from_numpy(tab.slot_expert.copy()).to(DEV),
+            "stamp": torch.from_numpy(tab.stamp.copy()).to(DEV),
+            "step": torch.from_numpy(tab.step.copy()).to(DEV)}
+    out = torch.zeros(K, dtype=torch.int32, device=DEV)
+    fs = torch.zeros(K, dtype=torch.int32, device=DEV)
+    fe = torch.zeros(K, dtype=torch.int32, device=DEV)
+    nm = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for i in range(ids_all.shape[0]):
+        _resolve(ids_all[i].contiguous(), tabs, out, fs, fe, nm, C, E)
+        want, wfs, wfe, n = oracle.resolve(tab, ids_all[i].cpu().numpy())
+        torch.cuda.synchronize()
+        assert int(nm.item()) == n, f"call {i}"
+        np.testing.assert_array_equal(out.cpu().numpy(), want)
+        np.testing.assert_array_equal(fs.cpu().numpy()[:n], wfs)
+        np.testing.assert_array_equal(fe.cpu().numpy()[:n], wfe)
+    np.testing.assert_array_equal(tabs["slot_of"].cpu().numpy(), tab.slot_of)
+    np.testing.assert_array_equal(tabs["slot_expert"].cpu().numpy(), tab.slot_expert)
+    np.testing.assert_array_equal(tabs["stamp"].cpu().numpy(), tab.stamp)
+    np.testing.assert_array_equal(tabs["step"].cpu().numpy(), tab.step)
+
+
 @pytest.fixture(scope="module")
 def pattern_host():
     """64 experts at the real dims, self-identifying bytes, pinned."""
