@@ -133,20 +133,15 @@ __device__ __forceinline__ void topk_select(const float (&v)[KPER], int per, int
   }
 }
 
-// bf16 bit pattern -> the same value as a double, by integer operations:
-// the sign, the exponent rebiased from 127 to 1023 and the 7 mantissa bits
-// placed at the top of the double's mantissa (zeros stay zeros).  Subnormal,
-// infinite and NaN inputs take the conversion instructions instead.  Exact
-// for every input.  Used where each converted weight feeds few products (the
-// decode kernel); where a staged token tile is converted per use the
-// conversion instructions measured faster.
-__device__ __forceinline__ double bf16_bits_to_f64(uint32_t b) {
-  const uint32_t e = b & 0x7f80u;
-  if (e == 0x7f80u || (e == 0u && (b & 0x7fu)))
-    return (double)__uint_as_float(b << 16);
-  const uint32_t mag = b & 0x7fffu;
-  const uint32_t hi = ((b & 0x8000u) << 16) | (mag ? (mag << 13) + (896u << 20) : 0u);
-  return __hiloint2double((int)hi, 0);
+// bf16 bit pattern (low 16 bits of b, or the high half of a packed pair
+// with hi = true) -> the same value as a double: the bits placed in the upper
+// half of an fp32 word ARE that value as an fp32 (same exponent range), and
+// fp32 -> fp64 is exact; one logic op and one conversion per value.
+// (Measured on B200 inside the decode router: the fp64 dot products of a
+// 16-SM cluster took 1.9 us this way against 3.8 us when the double was
+// assembled from the bits by ~12 integer operations.)
+__device__ __forceinline__ double bf16_bits_to_f64(uint32_t b, bool hi = false) {
+  return (double)__uint_as_float(hi ? (b & 0xffff0000u) : (b << 16));
 }
 
 // ---- decode batches (T <= 2): one cluster of 16 CTAs, no global scratch
@@ -235,8 +230,8 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
       double* dst = xd + (size_t)c * kRouterXChunk;   // chunk c of token c / vec
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        dst[2 * j] = bf16_bits_to_f64(qq[j] & 0xffffu);
-        dst[2 * j + 1] = bf16_bits_to_f64(qq[j] >> 16);
+        dst[2 * j] = bf16_bits_to_f64(qq[j]);
+        dst[2 * j + 1] = bf16_bits_to_f64(qq[j], true);
       }
     }
   } else {
@@ -267,8 +262,8 @@ __global__ void __launch_bounds__(kRouterClusterThreads, 1) router_cluster_kerne
         double wd[8];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          wd[2 * q] = bf16_bits_to_f64(wr[q] & 0xffffu);
-          wd[2 * q + 1] = bf16_bits_to_f64(wr[q] >> 16);
+          wd[2 * q] = bf16_bits_to_f64(wr[q]);
+          wd[2 * q + 1] = bf16_bits_to_f64(wr[q], true);
         }
 #pragma unroll
         for (int t = 0; t < kRouterClusterMaxT; ++t) {
