@@ -186,7 +186,8 @@ __device__ __forceinline__ void warp_argmin(int64_t& key, int& idx) {
 // so the prefetch is one memory round trip: with slot_of_smem the whole
 // slot_of table is staged alongside the ids instead of looked up by them.
 // Dynamic shared memory: stamp[C] (+ freq[C], ins[C] for LFU) int64, then
-// owner[C] int32, then (slot_of_smem) slot_of[num_experts] int32.
+// owner[C] int32, then (slot_of_smem) slot_of[num_experts] int32, then the
+// fast path's marks[C] bytes.
 __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   extern __shared__ int64_t sh[];
   const int C = p.capacity;
@@ -278,7 +279,72 @@ __global__ void __launch_bounds__(32) resolve_kernel(ResolveParams p) {
   __syncwarp();
   int out_lo = -1, out_hi = -1;
   int nmiss = 0, hits = 0;
-  for (int i = 0; i < p.k; ++i) {
+  // ---- LRU fast path (k <= 32 ids, one per lane; k < C; 32-bit keys): every
+  // hit at once, then the misses' victims in id order by repeated warp
+  // arg-min over the slots no hit of this call uses.  The sequential rule
+  // gives a miss the oldest slot not touched BEFORE it; this gives it the
+  // oldest slot not touched at all -- the same slot unless a slot hit later
+  // in the call is older than a victim, which the check below detects (then
+  // the sequential loop decides the call instead).  Duplicate ids take their
+  // first occurrence's slot, as the sequential walk's later lookups do.
+  bool fast_done = false;
+  if (!lfu && key32 && p.k <= 32 && p.k < C) {
+    uint8_t* s_mark = reinterpret_cast<uint8_t*>(s_slot_of + (p.slot_of_smem ? n : 0));  // [C]
+    __shared__ int s_vict[32];
+    const bool valid = lane < p.k && e_lo >= 0;
+    const unsigned same = __match_any_sync(full, valid ? e_lo : -1 - lane);
+    const int first = __ffs(same) - 1;
+    const bool isfirst = valid && first == lane;
+    const bool hit = isfirst && pre_lo >= 0 && s_owner[pre_lo] == e_lo;
+    for (int c = lane; c < C; c += 32) s_mark[c] = 0;
+    __syncwarp();
+    if (hit) s_mark[pre_lo] = 1;
+    __syncwarp();
+    const unsigned missmask = __ballot_sync(full, isfirst && !hit);
+    const int nm = __popc(missmask), nh = __popc(__ballot_sync(full, hit));
+    bool ok = nm <= C - nh;
+    int vkey = INT32_MIN, vidx = -1;   // the last (newest) victim's (stamp, slot)
+    for (int r = 0; ok && r < nm; ++r) {
+      int key = INT32_MAX, bi = INT32_MAX;
+      for (int c = lane; c < C; c += 32) {
+        const int v = (int)s_stamp[c];
+        if (s_mark[c] == 0 && v < key) { key = v; bi = c; }
+      }
+      vkey = __reduce_min_sync(full, key);
+      vidx = __reduce_min_sync(full, key == vkey ? bi : INT32_MAX);
+      if (lane == 0) { s_vict[r] = vidx; s_mark[vidx] = 2; }
+      __syncwarp();
+    }
+    if (ok && nm > 0) {
+      bool conflict = false;
+      if (hit) {
+        const int hs = (int)s_stamp[pre_lo];
+        conflict = hs < vkey || (hs == vkey && pre_lo < vidx);
+      }
+      ok = !__any_sync(full, conflict);
+    }
+    if (ok) {
+      const int rank = __popc(missmask & ((1u << lane) - 1u));
+      int s = hit ? pre_lo : (isfirst ? s_vict[rank] : -1);
+      const int sf = __shfl_sync(full, s, first);
+      if (valid && !isfirst) s = sf;
+      if (lane < p.k) p.out_slot[lane] = s;
+      if (isfirst) p.stamp[s] = step;
+      if (isfirst && !hit) {
+        const int32_t victim = s_owner[s];
+        if (victim >= 0) p.slot_of[victim] = -1;
+        p.slot_of[e_lo] = s;
+        p.slot_expert[s] = e_lo;
+        p.fetch_slot[rank] = s;
+        p.fetch_expert[rank] = e_lo;
+      }
+      nmiss = nm;
+      hits = __popc(__ballot_sync(full, valid)) - nm;
+      fast_done = true;
+    }
+    __syncwarp();
+  }
+  for (int i = 0; i < p.k && !fast_done; ++i) {
     const int src = i & 31;
     const int32_t e = __shfl_sync(full, i < 32 ? e_lo : e_hi, src);
     int32_t s = __shfl_sync(full, i < 32 ? pre_lo : pre_hi, src);
@@ -518,6 +584,7 @@ static int launch_resolve(ResolveParams p, cudaStream_t st) {
   const size_t slot_of_bytes = (size_t)p.num_experts * sizeof(int32_t);
   p.slot_of_smem = smem + slot_of_bytes <= 64 * 1024 ? 1 : 0;
   if (p.slot_of_smem) smem += slot_of_bytes;
+  smem += (size_t)p.capacity;   // the LRU fast path's per-slot marks
   if (smem > 48 * 1024) {
     D3_CUDA_TRY(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),
