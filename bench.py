@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--policy", choices=("lru", "lfu"), default="lru")
     ap.add_argument("--no-overlap", action="store_true",
                     help="decode: separate fetch and gate/up launches")
+    ap.add_argument("--one-host-copy", action="store_true",
+                    help="decode: one copy of the host store for all local ranks instead of "
+                         "one per NUMA node of their GPUs")
     ap.add_argument("--fetch-ctas", type=int, default=0)
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--cpu-layers", type=int, default=8,
@@ -279,7 +282,8 @@ def run_decode(args, rank, world, local):
     # its own offset (independent token streams)
     stack = DecodeStack(layers=args.layers, cache_gib=args.cache_gib, device=dev,
                         policy=args.policy, group=local_group(world), local_rank=local,
-                        trace_offset=512 * rank, overlap=not args.no_overlap)
+                        trace_offset=512 * rank, overlap=not args.no_overlap,
+                        host_per_node=not args.one_host_copy)
     from drama3_offloading_b200 import devcache
     devcache.FETCH_CTAS = args.fetch_ctas
     if args.fetch_ctas > 0:
@@ -335,6 +339,16 @@ def run_decode(args, rank, world, local):
     stack.restore(window)
     ft = stack.sample_fetch_timing(args.steps)
     fetch_gbs = ft["bytes"] / (ft["ms"] * 1e-3) / 1e9 if ft["ms"] > 0 else 0.0
+    hs = stack.store.host
+    host_store = {"copies": hs.copies, "gpu_nodes": [hs.rank_nodes[r] for r in sorted(hs.rank_nodes)],
+                  "node": hs.node, "bound": bool(hs.bound)}
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([fetch_gbs, float(bool(hs.bound))], dtype=torch.float64, device=dev)
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        host_store["fetch_gbs_per_rank"] = [round(float(x[0]), 2) for x in out]
+        host_store["bound_per_rank"] = [bool(x[1]) for x in out]
     hbm = measured_peaks()
     roof_ms = stack.roofline_ms(hits, misses, hbm["hbm_gbs"], peak["gbs"])
     return {"value": value, "ms": ms_max, "e2e": e2e, "e2e_steps": e2e_steps,
@@ -342,7 +356,7 @@ def run_decode(args, rank, world, local):
             "hits": hits, "misses": misses, "fetch_gbs": fetch_gbs, "fetch_sample": ft,
             "roof_ms": roof_ms, "hbm": hbm, "capacity": stack.capacity,
             "launches": stack.launches_per_step() * args.steps, "trace": stack.trace_dev.cpu().numpy(),
-            "dense_bytes": stack.dense_bytes}
+            "dense_bytes": stack.dense_bytes, "host_store": host_store}
 
 
 # ---------------------------------------------------------------- fetch
@@ -1054,6 +1068,7 @@ def main():
                         "window": f"the timed window from the same state ({r['e2e_steps']} "
                                   "steps), host sync every token"},
                 "clocks": r["clk"], "gpu_launches": r["launches"],
+                "host_store": r["host_store"],
             }
         if ep_rec is not None:
             line["ep"] = {k: ep_rec[k] for k in (

@@ -77,14 +77,15 @@ class DecodeStack:
                  dense_gib: float = DENSE_GIB, trace: np.ndarray | None = None, device="cuda",
                  policy: str = "lru", seed: int = 0, fill: str = "random", group=None,
                  local_rank: int = 0, trace_offset: int = 0, overlap: bool = True,
-                 kv_context: int = KV_CONTEXT):
+                 kv_context: int = KV_CONTEXT, host_per_node: bool = True):
         self.device = dev = torch.device(device)
         self.overlap = overlap
         self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
         per_expert = 2 * inter * hidden + hidden * inter + 4 * (2 * inter * hidden + hidden * inter) // (128 * 128)
         self.capacity = capacity or max(1, int(cache_gib * (1 << 30)) // (layers * per_expert))
         self.store = OffloadedExperts(layers, experts, hidden, inter, self.capacity, dev, seed,
-                                      policy, fill, group=group, local_rank=local_rank)
+                                      policy, fill, group=group, local_rank=local_rank,
+                                      per_node=host_per_node)
         self.trace_offset = trace_offset
         g = torch.Generator(device=dev).manual_seed(seed + 7)
         # the shared expert of every layer (bf16 gate/up [2I, H], down [H, I],

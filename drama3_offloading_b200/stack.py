@@ -6,8 +6,9 @@ pin_experts; bin/devcache.py:280-301 install_dev_cache).
 Weights are random-init (no checkpoint): N(0, 0.02) quantised per 128x128
 block, generated on the GPU a few experts at a time and copied into the host
 store.  The store is one shared, page-locked allocation per machine
-(``hoststore.SharedHostStore``): local rank 0 fills it, every local rank maps
-it and keeps its own device cache.
+(``hoststore.SharedHostStore``), one copy per NUMA node holding the ranks'
+GPUs: local rank 0 fills its copy, the owners of the other nodes' copies copy
+it, every local rank maps its node's copy and keeps its own device cache.
 """
 from __future__ import annotations
 
@@ -16,7 +17,7 @@ import time
 import torch
 
 from . import devcache, synth
-from .hoststore import SharedHostStore, layer_bytes
+from .hoststore import SharedHostStore, gpu_numa_node, layer_bytes
 
 GiB = 1 << 30
 
@@ -48,18 +49,19 @@ class OffloadedExperts:
     """``layers`` host expert stores (one shared page-locked allocation), each
     with its own device cache on ``device``.
 
-    ``group``/``local_rank``: the ranks of this machine share one store; local
-    rank 0 fills it."""
+    ``group``/``local_rank``: the ranks of this machine share the store (one
+    copy per NUMA node of their GPUs, ``per_node``); local rank 0 fills it."""
 
     def __init__(self, layers: int = 40, experts: int = 256, hidden: int = 2048,
                  inter: int = 512, capacity: int = 51, device="cuda", seed: int = 0,
-                 policy: str = "lru", fill: str = "random", group=None, local_rank: int = 0):
+                 policy: str = "lru", fill: str = "random", group=None, local_rank: int = 0,
+                 per_node: bool = True):
         import torch.distributed as dist
         self.device = torch.device(device)
         self.H, self.I, self.E = hidden, inter, experts
         t0 = time.perf_counter()
         self.host = SharedHostStore(layers * layer_bytes(experts, hidden, inter), local_rank,
-                                    group)
+                                    group, node=gpu_numa_node(self.device), per_node=per_node)
         self.layers = []
         for l in range(layers):
             ex = synth.HostExperts(
@@ -70,15 +72,22 @@ class OffloadedExperts:
                 self.host.take((experts, hidden // 128, inter // 128), torch.float32))
             self.layers.append(ex)
         multi = group is not None and dist.is_initialized() and dist.get_world_size(group) > 1
-        # the owner page-locks and fills first; the others page-lock the
-        # already-filled pages after the barrier
-        if self.host.owner:
+        # local rank 0 page-locks and fills its copy first; the owners of the
+        # other nodes' copies copy it and page-lock theirs; the other ranks
+        # page-lock their node's filled copy last
+        if self.host.primary:
             self.host.register()
             for l, ex in enumerate(self.layers):
                 fill_layer(ex, seed + l, self.device, fill)
         torch.cuda.synchronize(self.device)
         if multi:
             dist.barrier(group=group, device_ids=[self.device.index])
+        if self.host.copies > 1:
+            if self.host.owner and not self.host.primary:
+                self.host.copy_from_primary()
+                self.host.register()
+            if multi:
+                dist.barrier(group=group, device_ids=[self.device.index])
         if not self.host.owner:
             self.host.register()
         self.setup_s = time.perf_counter() - t0

@@ -86,3 +86,73 @@ def test_store_larger_than_ram_is_refused_on_every_rank():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: "refused", 1: "refused"}, res
+
+
+def _node_worker(rank, world, port, q, nodes, node_free):
+    """Ranks whose GPUs sit on ``nodes`` (faked), each node reporting
+    ``node_free`` free bytes."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from drama3_offloading_b200 import hoststore
+        hoststore.node_mem_free = lambda n: node_free
+        st = hoststore.SharedHostStore(1 << 20, local_rank=rank, group=dist.group.WORLD,
+                                       headroom=0, node=nodes[rank])
+        a = st.take((256,), torch.int64)
+        if st.primary:
+            a.copy_(torch.arange(256) * 7)
+        dist.barrier()
+        if st.copies > 1:
+            st.copy_from_primary()
+            dist.barrier()
+        same = bool((a == torch.arange(256) * 7).all())
+        dist.barrier()
+        # the last rank writes its copy; who sees it tells which ranks share it
+        if rank == world - 1:
+            a[0] = -1
+        dist.barrier()
+        q.put((rank, (st.copies, st.owner, same, int(a[0]) == -1)))
+    except Exception as exc:  # reported to the parent
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_nodes(nodes, node_free):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = len(nodes)
+    procs = [ctx.Process(target=_node_worker, args=(r, world, port, q, nodes, node_free))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+def test_one_copy_per_numa_node():
+    # GPUs on nodes 0, 1, 1: two copies with the same bytes; rank 2 shares
+    # rank 1's copy (its write is seen by rank 1, not by rank 0)
+    res = _run_nodes([0, 1, 1], 1 << 40)
+    assert res == {0: (2, True, True, False), 1: (2, True, True, True),
+                   2: (2, False, True, True)}, res
+
+
+def test_one_copy_when_nodes_unknown_or_short_of_ram():
+    # a node that cannot hold a copy, or a GPU whose node is unknown: one copy
+    for nodes, free in (([0, 1], 1 << 20), ([-1, 0], 1 << 40)):
+        res = _run_nodes(nodes, free)
+        assert res == {0: (1, True, True, True), 1: (1, False, True, True)}, (nodes, res)
+
+
+def test_single_rank_store_places_on_its_node():
+    from drama3_offloading_b200.hoststore import SharedHostStore
+    st = SharedHostStore(1 << 20, headroom=0, node=0)
+    a = st.take((4096,), torch.uint8)
+    a.fill_(3)
+    assert st.copies == 1 and st.owner and st.primary and st.node == 0
+    assert isinstance(st.bound, bool) and int(a.sum()) == 3 * 4096
