@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--ep-ranks", type=int, default=8,
                     help="ep-rank workload: the N whose per-rank expert call is emulated")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
+    ap.add_argument("--no-prefetch", action="store_true",
+                    help="prefill: gather each layer's union after its router (no gather of the "
+                         "next layer during this layer's GEMM)")
     ap.add_argument("--global-batch", type=int, default=64, help="ep workload: decode streams")
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--slots", type=int, default=2048, help="fetch workload: slots over all layers")
@@ -459,6 +462,8 @@ def run_prefill(args, rank, world, local):
     wts = torch.empty(T, 8, dtype=torch.float32, device=dev)
     rids = torch.empty(T, 8, dtype=torch.int32, device=dev)
 
+    pf = None if args.no_prefetch else offload.ChunkPrefetch(store.layers, dev)
+
     def step(events=None):
         h.copy_(h0)
         for l, ex in enumerate(store.layers):
@@ -466,7 +471,8 @@ def run_prefill(args, rank, world, local):
             if events is not None:
                 e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
                 e0.record()
-            y = offload.offloaded_forward(ex, h, ids[l], wts)
+            y = (offload.offloaded_forward(ex, h, ids[l], wts) if pf is None
+                 else pf.forward(l, h, ids[l], wts))
             if events is not None:
                 e1.record()
                 events.append((e0, e1))
@@ -515,14 +521,20 @@ def run_prefill(args, rank, world, local):
         "data": "synthetic (random-init FP8 experts, Zipf(1.1) top-8 per token)",
         "config": {"workload": "prefill-gather", "tokens": T, "layers": args.layers,
                    "cache_slots_per_layer": cap, "parallelism": f"replicas{world}",
-                   "l2": "inputs > L2"},
+                   "l2": "inputs > L2",
+                   "prefetch": ("none: each layer's union gathered after its router"
+                                if pf is None or not pf._piped else
+                                "every expert of the next layer gathered during this layer's "
+                                "GEMM (side stream, two full-layer buffers)")},
         "experts_fetched_per_chunk": fetched, "experts_borrowed_per_chunk": borrowed,
         "gather_gbs": fetch_gbs, "host_link_peak_gbs": peak["gbs"],
         "roofline": {"bound": "host_link", "kernel": "gather_kernel (fetch of the union's misses)",
                      "achieved": fetch_gbs, "peak": peak["gbs"], "unit": "GB/s",
                      "frac": fetch_gbs / peak["gbs"], "traffic": None},
         "moe_ms_per_chunk": layer_ms, "moe_tflops": flops / (layer_ms * 1e-3) / 1e12,
-        "clocks": clk.summary(), "gpu_launches": args.steps * args.layers * 9,
+        "clocks": clk.summary(),
+        # per layer: router, plan (union path only), gather, and the expert call's launches
+        "gpu_launches": args.steps * args.layers * (9 if pf is None or not pf._piped else 8),
     }
 
 

@@ -224,6 +224,91 @@ def offloaded_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
     return moe.fp8_moe_forward(x, local, topk_weights, b["w13"], b["s13"], b["w2"], b["s2"])
 
 
+class ChunkPrefetch:
+    """Prefill-chunk pipeline over a stack of offloaded layers: while layer
+    l's expert GEMM runs, every expert of layer l+1 is gathered (cached ones
+    borrowed read-only from that layer's device cache, the rest fetched from
+    pinned host) into the other of two full-layer buffers, on a side stream.
+
+    A 2048-token chunk routes top-8 to every one of the 256 experts of a layer
+    (its union is the whole layer), so gathering the whole next layer fetches
+    exactly the bytes the union gather of ``offloaded_forward`` would; the
+    host link then never waits for a GEMM.  Below ``min_pairs_per_expert``
+    routed pairs per expert (where the union is a fraction of the layer)
+    ``forward`` falls back to ``offloaded_forward``.  Expert e sits at row e
+    of the full-layer buffers, so the GEMM takes the routed ids as they are
+    and gives the same bits as the union gather (whose compact numbering the
+    GEMM's results do not depend on).
+
+    Use: ``pf = ChunkPrefetch(layers)``; per chunk, for every layer in order,
+    ``y = pf.forward(l, x, topk_ids, topk_weights)``.  Graph-capturable (the
+    side stream forks from and joins the calling stream within each chunk).
+    The reference gathers each layer's union after its router
+    (bin/offload.py:186-226); it has no cross-layer prefetch."""
+
+    def __init__(self, layers, device=None, fetch_ctas: int = 64,
+                 min_pairs_per_expert: float = 4.0):
+        self.layers = list(layers)
+        ex0 = self.layers[0]
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        self.E = ex0.num_experts
+        self.bufs = []
+        for _ in range(2):
+            b = {"w13": torch.empty(ex0.w13_weight.shape, dtype=ex0.w13_weight.dtype, device=dev),
+                 "w2": torch.empty(ex0.w2_weight.shape, dtype=ex0.w2_weight.dtype, device=dev),
+                 "s13": torch.empty(ex0.w13_scale_inv.shape, dtype=torch.float32, device=dev),
+                 "s2": torch.empty(ex0.w2_scale_inv.shape, dtype=torch.float32, device=dev)}
+            b["dst"] = (ctypes.c_void_p * 4)(*(b[n].data_ptr() for n in ("w13", "w2", "s13", "s2")))
+            self.bufs.append(b)
+        self.all = torch.arange(self.E, dtype=torch.int32, device=dev)
+        self.n = torch.full((1,), self.E, dtype=torch.int32, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        L = len(self.layers)
+        self.ev_gathered = [torch.cuda.Event() for _ in range(L)]
+        self.ev_used = [torch.cuda.Event() for _ in range(L)]
+        self.fetch_ctas = int(fetch_ctas)
+        self.min_pairs_per_expert = float(min_pairs_per_expert)
+        self._piped = False
+        for ex in self.layers:
+            if getattr(ex, "_d3_gather_counters", None) is None:
+                ex._d3_gather_counters = torch.zeros(2, dtype=torch.int64, device=dev)
+
+    def _gather(self, l: int) -> None:
+        ex = self.layers[l]
+        b = self.bufs[l % 2]
+        _lib.call("d3_gather_experts", ctypes.byref(_layer_desc(ex)), _lib.ptr(self.all),
+                  _lib.ptr(self.n), b["dst"], _lib.ptr(ex._d3_gather_counters), self.fetch_ctas,
+                  _lib.stream_ptr(self.side))
+        self.ev_gathered[l].record(self.side)
+
+    def forward(self, l: int, x, topk_ids, topk_weights):
+        """Layer l's MoE output for the chunk (layers in order, l = 0 first)."""
+        ex = self.layers[l]
+        if ex.w13_weight.device.type != "cpu":
+            return offloaded_forward(ex, x, topk_ids, topk_weights)
+        if l == 0:
+            self._piped = topk_ids.numel() >= self.min_pairs_per_expert * self.E
+        if not self._piped:
+            return offloaded_forward(ex, x, topk_ids, topk_weights)
+        main = torch.cuda.current_stream(self.device)
+        if l == 0:
+            self.side.wait_stream(main)
+            self._gather(0)
+        if l + 1 < len(self.layers):
+            if l >= 1:
+                # the buffer layer l+1 lands in was read by layer l-1's GEMM
+                self.side.wait_event(self.ev_used[l - 1])
+            self._gather(l + 1)
+        main.wait_event(self.ev_gathered[l])
+        observe(ex, topk_ids)
+        b = self.bufs[l % 2]
+        y = moe.fp8_moe_forward(x, topk_ids, topk_weights, b["w13"], b["s13"], b["w2"], b["s2"])
+        self.ev_used[l].record(main)
+        return y
+
+
 def offloaded_stores(source) -> list:
     """The expert stores that live in host memory.  ``source`` is a model in
     the reference's layout (``model.backbone.model.layers[i].mlp.experts``:

@@ -118,3 +118,65 @@ def test_offloaded_forward_equals_resident(T, cap):
     if cap:
         got2 = devcache.dev_cached_forward(host, x, ids, w)
         assert torch.equal(got2, want)
+
+
+@pytest.mark.parametrize("T", [300, 5])
+def test_chunk_prefetch_equals_union_gather(T):
+    """Three offloaded layers with warm caches: the cross-layer prefetch
+    pipeline (offload.ChunkPrefetch) gives the same bits as gathering each
+    layer's union after its router, eagerly and replayed from a CUDA graph;
+    T = 5 (40 pairs for 64 experts) takes the union path inside it."""
+    E, L = 64, 3
+    layers = []
+    for l in range(L):
+        host = synth.make_experts(E, seed=20 + l, device="cuda").to("cpu").pin()
+        devcache.init_dev_cache(host, DEV, 16)
+        devcache.dev_resolve_and_fetch(host, torch.randperm(E)[:8 + l].to(DEV))
+        layers.append(host)
+    torch.cuda.synchronize()
+    g = torch.Generator().manual_seed(T)
+    x0 = torch.randn(T, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    ids = [torch.stack([torch.randperm(E, generator=g)[:8] for _ in range(T)]).to(DEV)
+           for _ in range(L)]
+    w = torch.rand(T, 8, generator=g)
+    w = (w / w.sum(-1, keepdim=True)).to(DEV)
+
+    def chunk(fwd, h):
+        h.copy_(x0)
+        for l in range(L):
+            h.add_(fwd(l, h, ids[l], w))
+        return h
+
+    want = chunk(lambda l, h, i, ww: offload.offloaded_forward(layers[l], h, i, ww),
+                 torch.empty_like(x0)).clone()
+    c0 = [offload.gather_counters(ex) for ex in layers]
+    pf = offload.ChunkPrefetch(layers, DEV)
+    got = chunk(pf.forward, torch.empty_like(x0)).clone()
+    moe.check_errors(DEV)
+    torch.cuda.synchronize()
+    assert pf._piped == (T * 8 >= 4 * E)
+    assert torch.equal(got, want)
+    if pf._piped:
+        # the whole layer was gathered: its resident experts borrowed, the rest fetched
+        for l, ex in enumerate(layers):
+            c1 = offload.gather_counters(ex)
+            resident = int((ex._dc_slot_of >= 0).sum())
+            assert c1["gather_hits"] - c0[l]["gather_hits"] == resident
+            assert c1["gather_misses"] - c0[l]["gather_misses"] == E - resident
+    # captured once, replayed twice
+    h = torch.empty_like(x0)
+    s = torch.cuda.Stream(device=DEV)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chunk(pf.forward, h)
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        chunk(pf.forward, h)
+    for _ in range(2):
+        h.zero_()
+        gr.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(h, want)
+    moe.check_errors(DEV)
+    del gr
