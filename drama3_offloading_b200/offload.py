@@ -9,6 +9,11 @@ parts of the reference's ``bin/offload.py``.
   with the ids remapped.  Unlike the reference (``torch.unique(ids.cpu())``, a
   host sync per layer, then one ``copy_`` per expert and buffer), the union,
   the remap and the gather are three device launches with static shapes.
+* ``ChunkPrefetch`` (no counterpart in the reference): for prefill chunks,
+  whose every layer routes to all of its experts, the next layer's experts are
+  gathered on a side stream while this layer's expert GEMM runs, so the host
+  link never waits for a GEMM; ``install_offload(..., chunk_prefetch=True)``
+  puts the installed forward on it.
 * ``STATS``, ``HYBRID_GATHER``, ``GATHER_DONE_HOOK``, ``EXPERT_BYTES``,
   ``pin_experts``, ``size_cache_to_free_vram``, ``install_offload`` keep the
   reference's names and meaning (:242-254, :603-704).
@@ -43,6 +48,9 @@ STATS = {"experts_copied": 0, "bytes_copied": 0, "hits": 0, "misses": 0,
          "gather_hits": 0, "gather_misses": 0}
 
 _BUF: dict = {}
+# install_offload(..., chunk_prefetch=True): the offloaded layers in model order
+# and their shared ChunkPrefetch (made on the first multi-row call)
+_CHAIN: dict = {"layers": [], "pf": None}
 
 
 # ---------------------------------------------------------------- trace
@@ -196,8 +204,23 @@ def gather_counters(experts) -> dict:
 
 
 def offloaded_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
-    """MoE forward for experts held in pinned host memory (any number of rows)."""
+    """MoE forward for experts held in pinned host memory (any number of rows).
+    Layers installed with ``install_offload(..., chunk_prefetch=True)`` run
+    through the model's shared ``ChunkPrefetch``."""
+    pos = getattr(self, "_d3_chain_pos", None)
+    if pos is not None and self.w13_weight.device.type == "cpu":
+        pf = _CHAIN["pf"]
+        if pf is None or pf.device != x.device:
+            pf = _CHAIN["pf"] = ChunkPrefetch(_CHAIN["layers"], x.device)
+        return pf.forward_in_order(pos, x, topk_ids, topk_weights)
     observe(self, topk_ids)
+    return _union_forward(self, x, topk_ids, topk_weights, fetch_ctas)
+
+
+def _union_forward(self, x, topk_ids, topk_weights, fetch_ctas: int = 0):
+    """The layer's union of routed experts gathered after its router (cached
+    ones borrowed read-only, the rest fetched), then the expert GEMM on the
+    compact set (bin/offload.py:186-226)."""
     if self.w13_weight.device.type != "cpu":
         return moe.fp8_moe_forward(x, topk_ids, topk_weights, self.w13_weight,
                                    self.w13_scale_inv, self.w2_weight, self.w2_scale_inv)
@@ -271,6 +294,7 @@ class ChunkPrefetch:
         self.fetch_ctas = int(fetch_ctas)
         self.min_pairs_per_expert = float(min_pairs_per_expert)
         self._piped = False
+        self._next = -1
         for ex in self.layers:
             if getattr(ex, "_d3_gather_counters", None) is None:
                 ex._d3_gather_counters = torch.zeros(2, dtype=torch.int64, device=dev)
@@ -286,12 +310,12 @@ class ChunkPrefetch:
     def forward(self, l: int, x, topk_ids, topk_weights):
         """Layer l's MoE output for the chunk (layers in order, l = 0 first)."""
         ex = self.layers[l]
-        if ex.w13_weight.device.type != "cpu":
-            return offloaded_forward(ex, x, topk_ids, topk_weights)
         if l == 0:
-            self._piped = topk_ids.numel() >= self.min_pairs_per_expert * self.E
-        if not self._piped:
-            return offloaded_forward(ex, x, topk_ids, topk_weights)
+            self._piped = (topk_ids.numel() >= self.min_pairs_per_expert * self.E
+                           and ex.w13_weight.device.type == "cpu")
+        if not self._piped or ex.w13_weight.device.type != "cpu":
+            observe(ex, topk_ids)
+            return _union_forward(ex, x, topk_ids, topk_weights)
         main = torch.cuda.current_stream(self.device)
         if l == 0:
             self.side.wait_stream(main)
@@ -307,6 +331,22 @@ class ChunkPrefetch:
         y = moe.fp8_moe_forward(x, topk_ids, topk_weights, b["w13"], b["s13"], b["w2"], b["s2"])
         self.ev_used[l].record(main)
         return y
+
+    def forward_in_order(self, l: int, x, topk_ids, topk_weights):
+        """``forward`` for callers that see one layer at a time (the installed
+        experts forward): layer 0 starts a chunk; a layer called out of order
+        gathers its own union, and so does every later layer of that chunk.
+        (Under stream capture an out-of-order call would leave the side
+        stream's last gather unjoined, which the capture rejects.)"""
+        if l == 0:
+            self._next = 0
+        if l != self._next:
+            self._next = -1
+            ex = self.layers[l]
+            observe(ex, topk_ids)
+            return _union_forward(ex, x, topk_ids, topk_weights)
+        self._next = l + 1
+        return self.forward(l, x, topk_ids, topk_weights)
 
 
 def offloaded_stores(source) -> list:
@@ -387,15 +427,25 @@ def size_cache_to_free_vram(model, device, leave_free_gib: float = 2.0,
     return capacity
 
 
-def install_offload(experts_cls, model=None) -> None:
+def install_offload(experts_cls, model=None, chunk_prefetch: bool = False) -> None:
     """Route ``experts_cls.forward`` through offloaded_forward, keeping the
     stock forward as ``_stock_forward`` (bin/offload.py:702-704).  With the
     model given, every layer's experts also get ``_layer_index`` (the census
-    and trace key, bin/offload.py:128)."""
+    and trace key, bin/offload.py:128); with ``chunk_prefetch`` too, the
+    offloaded layers share one ``ChunkPrefetch`` (multi-row calls gather the
+    next layer's experts during this layer's GEMM; two full-layer buffers of
+    device memory, ~1.6 GB at Drama-3's shapes, made on the first such call)."""
     experts_cls._stock_forward = experts_cls.forward
     experts_cls.forward = offloaded_forward
     if model is not None:
+        chain = []
         for index, layer in enumerate(model.backbone.model.layers):
             experts = getattr(layer.mlp, "experts", None)
             if experts is not None:
                 experts._layer_index = index
+                if chunk_prefetch:
+                    experts._d3_chain_pos = len(chain)
+                    chain.append(experts)
+        if chunk_prefetch:
+            _CHAIN["layers"] = chain
+            _CHAIN["pf"] = None

@@ -180,3 +180,55 @@ def test_chunk_prefetch_equals_union_gather(T):
         assert torch.equal(h, want)
     moe.check_errors(DEV)
     del gr
+
+
+def test_installed_forward_runs_the_chunk_pipeline():
+    """install_offload(..., chunk_prefetch=True): the experts' own forward,
+    called layer by layer as the model does, runs the cross-layer pipeline
+    with the union gather's bits; a layer called out of order gathers its
+    union."""
+    from types import SimpleNamespace
+
+    class _Experts(synth.HostExperts):
+        pass
+
+    E, L, T = 64, 3, 300
+    layers = []
+    for l in range(L):
+        h = synth.make_experts(E, seed=30 + l, device="cuda").to("cpu").pin()
+        ex = _Experts(E, h.w13_weight, h.w2_weight, h.w13_scale_inv, h.w2_scale_inv)
+        devcache.init_dev_cache(ex, DEV, 16)
+        devcache.dev_resolve_and_fetch(ex, torch.randperm(E)[:8].to(DEV))
+        layers.append(ex)
+    g = torch.Generator().manual_seed(11)
+    x0 = torch.randn(T, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    ids = [torch.stack([torch.randperm(E, generator=g)[:8] for _ in range(T)]).to(DEV)
+           for _ in range(L)]
+    w = torch.rand(T, 8, generator=g)
+    w = (w / w.sum(-1, keepdim=True)).to(DEV)
+
+    def chunk(fwd):
+        h = x0.clone()
+        for l in range(L):
+            h.add_(fwd(l, h, ids[l], w))
+        return h
+
+    want = chunk(lambda l, h, i, ww: offload.offloaded_forward(layers[l], h, i, ww)).clone()
+    want1 = offload.offloaded_forward(layers[1], x0, ids[1], w).clone()
+    model = SimpleNamespace(backbone=SimpleNamespace(model=SimpleNamespace(
+        layers=[SimpleNamespace(mlp=SimpleNamespace(experts=ex)) for ex in layers])))
+    offload.install_offload(_Experts, model, chunk_prefetch=True)
+    try:
+        got = chunk(lambda l, h, i, ww: layers[l].forward(h, i, ww))
+        torch.cuda.synchronize()
+        pf = offload._CHAIN["pf"]
+        assert pf is not None and pf._piped
+        assert torch.equal(got, want)
+        got1 = layers[1].forward(x0, ids[1], w)
+        assert pf._next == -1
+        assert torch.equal(got1, want1)
+        moe.check_errors(DEV)
+    finally:
+        offload._CHAIN.update(layers=[], pf=None)
+        for ex in layers:
+            del ex._d3_chain_pos
