@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--one-host-copy", action="store_true",
                     help="decode: one copy of the host store for all local ranks instead of "
                          "one per NUMA node of their GPUs")
+    ap.add_argument("--l2-warm-mib", type=float, default=85.0,
+                    help="decode: MiB of the next layer's first dense weight hinted into L2 "
+                         "during each layer's fetch (85 = all of it; 0 = off)")
     ap.add_argument("--fetch-ctas", type=int, default=0)
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--cpu-layers", type=int, default=8,
@@ -251,7 +254,7 @@ def decode_config(args, capacity: int | None = None) -> dict:
     return {"workload": "decode-40L-bs1-offloaded", "layers": args.layers, "hidden": 2048,
             "experts": 256, "topk": 8, "shared_expert": True, "cache_gib": args.cache_gib,
             "slots_per_layer": cap, "policy": args.policy, "fetch_overlap": not args.no_overlap,
-            "kv_context": dec.KV_CONTEXT,
+            "kv_context": dec.KV_CONTEXT, "l2_warm_mib": args.l2_warm_mib,
             "kv_mib_per_token": len(dec.full_attention_layers(args.layers)) * 2 *
             dec.KV_CONTEXT * dec.KV_HEADS * dec.HEAD_DIM * 2 / 2**20,
             "dense_gib_per_token": dense / 2**30,
@@ -286,7 +289,7 @@ def run_decode(args, rank, world, local):
     stack = DecodeStack(layers=args.layers, cache_gib=args.cache_gib, device=dev,
                         policy=args.policy, group=local_group(world), local_rank=local,
                         trace_offset=512 * rank, overlap=not args.no_overlap,
-                        host_per_node=not args.one_host_copy)
+                        host_per_node=not args.one_host_copy, l2_warm_mib=args.l2_warm_mib)
     from drama3_offloading_b200 import devcache
     devcache.FETCH_CTAS = args.fetch_ctas
     if args.fetch_ctas > 0:

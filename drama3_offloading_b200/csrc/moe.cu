@@ -869,6 +869,8 @@ struct FetchOverlapParams {
   int* err;
   int err_code;
   unsigned long long budget_ns;
+  const char* warm;                // optional: static bytes to warm into L2 (next layer's weights)
+  unsigned long long warm_lines;   // 128-byte lines of them
 };
 
 __device__ __forceinline__ void overlap_vec(const FetchParams& f, uint32_t mask, bool early,
@@ -968,6 +970,17 @@ __global__ void __launch_bounds__(kGemvThreads) fetch_gemv13_kernel(FetchParams 
   const long gw = ((long)(blockIdx.x - o.fetch_ctas) * blockDim.x + threadIdx.x) >> 5;
   const long nw = ((long)(gridDim.x - o.fetch_ctas) * blockDim.x) >> 5;
   gemv13_units<CPL>(p, gw, nw, &ov);
+  // With a warm window: once its units are done, each gate/up thread hints
+  // its share of the window's lines into L2 (a hint, nothing waits on it),
+  // while the fetch CTAs still hold the host link.  The window is static
+  // weights the next launches read (the next layer's dense weights), so HBM,
+  // idle during the host-bound fetch, serves them ahead of time.
+  if (o.warm_lines) {
+    const unsigned long long t =
+        (unsigned long long)(blockIdx.x - o.fetch_ctas) * blockDim.x + threadIdx.x;
+    const unsigned long long nt = (unsigned long long)(gridDim.x - o.fetch_ctas) * blockDim.x;
+    for (unsigned long long i = t; i < o.warm_lines; i += nt) prefetch_l2(o.warm + (i << 7));
+  }
 }
 
 constexpr uint64_t kOverlapWaitBudgetNs = 2000000000ull;
@@ -1305,13 +1318,15 @@ size_t d3_resolve_fetch_moe_workspace_size(int32_t k, int32_t H, int32_t I) {
   return overlap_workspace(k, I);
 }
 
-int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
-                         const void* x, const void* weights, int32_t weights_f32, int32_t H,
-                         int32_t I, const void* shared_w13, const void* shared_w2,
-                         const void* shared_gate, void* out, int32_t accumulate,
-                         int32_t* err_word, void* workspace, size_t workspace_bytes,
-                         int32_t fetch_ctas, int32_t stages, d3_stream_t stream) {
+static int resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_bytes,
+                             int32_t k, const void* x, const void* weights, int32_t weights_f32,
+                             int32_t H, int32_t I, const void* shared_w13, const void* shared_w2,
+                             const void* shared_gate, void* out, int32_t accumulate,
+                             int32_t* err_word, void* workspace, size_t workspace_bytes,
+                             int32_t fetch_ctas, int32_t stages, const void* l2_warm,
+                             size_t l2_warm_bytes, d3_stream_t stream) {
   D3_CHECK_ARG(L && ids && x && weights && out && err_word, "d3_resolve_fetch_moe: null pointer");
+  D3_CHECK_ARG(l2_warm || !l2_warm_bytes, "d3_resolve_fetch_moe_l2warm: null window");
   D3_CHECK_ARG(stages >= 1 && stages <= 7, "stages must be a non-empty mask of 1, 2, 4");
   D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
   if (!gemv_shapes_ok(k, H, I))
@@ -1375,6 +1390,8 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   o.early_mask = (1u << 0) | (1u << 2);
   o.vecA = (b13 + bs13) / 16;
   o.err = err_word; o.err_code = 41; o.budget_ns = kOverlapWaitBudgetNs;
+  o.warm = static_cast<const char*>(l2_warm);
+  o.warm_lines = (unsigned long long)(l2_warm_bytes >> 7);
   const int grid = 2 * num_sms();
   cudaError_t e;
   const bool pdl = pdl_enabled() && (stages & 1);
@@ -1386,6 +1403,30 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
   }
   D3_CUDA_TRY(e, "fetch_gemv13_kernel launch");
   return (stages & 4) ? run_gemv2(gp, st, pdl_enabled()) : D3_OK;
+}
+
+int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_bytes, int32_t k,
+                         const void* x, const void* weights, int32_t weights_f32, int32_t H,
+                         int32_t I, const void* shared_w13, const void* shared_w2,
+                         const void* shared_gate, void* out, int32_t accumulate,
+                         int32_t* err_word, void* workspace, size_t workspace_bytes,
+                         int32_t fetch_ctas, int32_t stages, d3_stream_t stream) {
+  return resolve_fetch_moe(L, ids, ids_bytes, k, x, weights, weights_f32, H, I, shared_w13,
+                           shared_w2, shared_gate, out, accumulate, err_word, workspace,
+                           workspace_bytes, fetch_ctas, stages, nullptr, 0, stream);
+}
+
+int d3_resolve_fetch_moe_l2warm(const d3_layer_cache* L, const void* ids, int32_t ids_bytes,
+                                int32_t k, const void* x, const void* weights,
+                                int32_t weights_f32, int32_t H, int32_t I,
+                                const void* shared_w13, const void* shared_w2,
+                                const void* shared_gate, void* out, int32_t accumulate,
+                                int32_t* err_word, void* workspace, size_t workspace_bytes,
+                                int32_t fetch_ctas, int32_t stages, const void* l2_warm,
+                                size_t l2_warm_bytes, d3_stream_t stream) {
+  return resolve_fetch_moe(L, ids, ids_bytes, k, x, weights, weights_f32, H, I, shared_w13,
+                           shared_w2, shared_gate, out, accumulate, err_word, workspace,
+                           workspace_bytes, fetch_ctas, stages, l2_warm, l2_warm_bytes, stream);
 }
 
 int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,

@@ -197,14 +197,18 @@ def dev_resolve_and_fetch(experts, topk_ids: torch.Tensor, stream=None) -> torch
 def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
                           topk_weights: torch.Tensor, out: torch.Tensor | None = None,
                           accumulate: bool = False, shared: tuple | None = None,
-                          stream=None, stages: int = 7) -> torch.Tensor:
+                          stream=None, stages: int = 7, l2_warm: torch.Tensor | None = None,
+                          l2_warm_bytes: int | None = None) -> torch.Tensor:
     """One decode row through the cache: resolve ``topk_ids`` [1, k], fetch the
     misses while the gate/up products of the resident experts run, then the
     down projection into ``out`` (bf16 [1, H]; added to it with
     ``accumulate``).  ``shared=(w13_s, w2_s, gate_s)`` adds the shared expert
     inside the same launches.  Sync-free and graph-capturable.  ``stages``
     masks the launches issued (1 allocator, 2 fetch + gate/up, 4 down
-    projection; 7 = all), to time them apart."""
+    projection; 7 = all), to time them apart.  ``l2_warm`` (a contiguous
+    device tensor of static weights the next launches read, e.g. the next
+    layer's dense weights): its first ``l2_warm_bytes`` (all by default) are
+    hinted into L2 while the fetch holds the host link."""
     from . import moe
     ids = _ids_arg(topk_ids)
     k = ids.numel()
@@ -227,14 +231,23 @@ def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
     if need == 0:
         raise ValueError(f"unsupported shape k={k} H={H} I={I}")
     ws = moe._workspace(x.device, need, "overlap")
-    _lib.call("d3_resolve_fetch_moe", ctypes.byref(experts._dc_desc), _lib.ptr(ids),
-              ids.element_size(), k, _lib.ptr(x), _lib.ptr(w),
-              1 if w.dtype == torch.float32 else 0, H, I,
-              _lib.ptr(sw13) if sw13 is not None else None,
-              _lib.ptr(sw2) if sw2 is not None else None,
-              _lib.ptr(sg) if sg is not None else None, _lib.ptr(out), 1 if accumulate else 0,
-              _lib.ptr(moe.error_word(x.device)), _lib.ptr(ws), ws.numel(),
-              int(OVERLAP_FETCH_CTAS), int(stages), _lib.stream_ptr(stream))
+    args = (ctypes.byref(experts._dc_desc), _lib.ptr(ids),
+            ids.element_size(), k, _lib.ptr(x), _lib.ptr(w),
+            1 if w.dtype == torch.float32 else 0, H, I,
+            _lib.ptr(sw13) if sw13 is not None else None,
+            _lib.ptr(sw2) if sw2 is not None else None,
+            _lib.ptr(sg) if sg is not None else None, _lib.ptr(out), 1 if accumulate else 0,
+            _lib.ptr(moe.error_word(x.device)), _lib.ptr(ws), ws.numel(),
+            int(OVERLAP_FETCH_CTAS), int(stages))
+    if l2_warm is None:
+        _lib.call("d3_resolve_fetch_moe", *args, _lib.stream_ptr(stream))
+    else:
+        if not l2_warm.is_cuda or not l2_warm.is_contiguous():
+            raise ValueError("l2_warm must be a contiguous device tensor")
+        nb = l2_warm.numel() * l2_warm.element_size()
+        nb = nb if l2_warm_bytes is None else max(0, min(nb, int(l2_warm_bytes)))
+        _lib.call("d3_resolve_fetch_moe_l2warm", *args, _lib.ptr(l2_warm), nb,
+                  _lib.stream_ptr(stream))
     return out
 
 
