@@ -75,6 +75,8 @@ def parse():
     ap.add_argument("--l2-warm-mib", type=float, default=85.0,
                     help="decode: MiB of the next layer's first dense weight hinted into L2 "
                          "during each layer's fetch (85 = all of it; 0 = off)")
+    ap.add_argument("--no-l2-warm-gate", action="store_true",
+                    help="decode: do not hint the next layer's router gate weight into L2")
     ap.add_argument("--fetch-ctas", type=int, default=0)
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--cpu-layers", type=int, default=8,
@@ -255,6 +257,7 @@ def decode_config(args, capacity: int | None = None) -> dict:
             "experts": 256, "topk": 8, "shared_expert": True, "cache_gib": args.cache_gib,
             "slots_per_layer": cap, "policy": args.policy, "fetch_overlap": not args.no_overlap,
             "kv_context": dec.KV_CONTEXT, "l2_warm_mib": args.l2_warm_mib,
+            "l2_warm_gate": not args.no_l2_warm_gate,
             "kv_mib_per_token": len(dec.full_attention_layers(args.layers)) * 2 *
             dec.KV_CONTEXT * dec.KV_HEADS * dec.HEAD_DIM * 2 / 2**20,
             "dense_gib_per_token": dense / 2**30,
@@ -289,7 +292,8 @@ def run_decode(args, rank, world, local):
     stack = DecodeStack(layers=args.layers, cache_gib=args.cache_gib, device=dev,
                         policy=args.policy, group=local_group(world), local_rank=local,
                         trace_offset=512 * rank, overlap=not args.no_overlap,
-                        host_per_node=not args.one_host_copy, l2_warm_mib=args.l2_warm_mib)
+                        host_per_node=not args.one_host_copy, l2_warm_mib=args.l2_warm_mib,
+                        l2_warm_gate=not args.no_l2_warm_gate)
     from drama3_offloading_b200 import devcache
     devcache.FETCH_CTAS = args.fetch_ctas
     if args.fetch_ctas > 0:

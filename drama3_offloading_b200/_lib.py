@@ -79,7 +79,7 @@ SIGNATURES: dict[str, tuple] = {
                                             I32, I32, P, P, P, P, I32, P, P, SZ, I32, I32, P]),
     "d3_resolve_fetch_moe_l2warm": (ctypes.c_int, [ctypes.POINTER(LayerCache), P, I32, I32, P, P,
                                                    I32, I32, I32, P, P, P, P, I32, P, P, SZ, I32,
-                                                   I32, P, SZ, P]),
+                                                   I32, P, P, I32, P]),
     "d3_moe_fp8_forward_p2p": (ctypes.c_int, [P, P, I32, P, I32, I32, I32, P, P, P, P, I32, I32,
                                               I32, P, P, SZ, P, P, I32, I32, I32, P, P, P, I32,
                                               I64, P]),

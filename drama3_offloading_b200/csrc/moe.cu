@@ -869,8 +869,12 @@ struct FetchOverlapParams {
   int* err;
   int err_code;
   unsigned long long budget_ns;
-  const char* warm;                // optional: static bytes to warm into L2 (next layer's weights)
-  unsigned long long warm_lines;   // 128-byte lines of them
+  // optional: up to kMaxWarmWindows ranges of static bytes to warm into L2
+  // (the next layer's weights), as 128-byte lines; warm_end[w] = lines of
+  // windows 0..w together
+  const char* warm[4];
+  unsigned long long warm_end[4];
+  int n_warm;
 };
 
 __device__ __forceinline__ void overlap_vec(const FetchParams& f, uint32_t mask, bool early,
@@ -975,15 +979,22 @@ __global__ void __launch_bounds__(kGemvThreads) fetch_gemv13_kernel(FetchParams 
   // while the fetch CTAs still hold the host link.  The window is static
   // weights the next launches read (the next layer's dense weights), so HBM,
   // idle during the host-bound fetch, serves them ahead of time.
-  if (o.warm_lines) {
+  if (o.n_warm > 0) {
     const unsigned long long t =
         (unsigned long long)(blockIdx.x - o.fetch_ctas) * blockDim.x + threadIdx.x;
     const unsigned long long nt = (unsigned long long)(gridDim.x - o.fetch_ctas) * blockDim.x;
-    for (unsigned long long i = t; i < o.warm_lines; i += nt) prefetch_l2(o.warm + (i << 7));
+    const unsigned long long total = o.warm_end[o.n_warm - 1];
+    int w = 0;
+    for (unsigned long long i = t; i < total; i += nt) {
+      while (i >= o.warm_end[w]) ++w;   // i < total = warm_end[n_warm - 1]: w stays in range
+      const unsigned long long first = w ? o.warm_end[w - 1] : 0ull;
+      prefetch_l2(o.warm[w] + ((i - first) << 7));
+    }
   }
 }
 
 constexpr uint64_t kOverlapWaitBudgetNs = 2000000000ull;
+constexpr int kMaxWarmWindows = 4;
 constexpr int kOverlapFetchCtas = 64;   // measured: 16 -> 80, 32 -> 102, 64 / 148 -> 103.7 tok/s
 
 static size_t overlap_workspace(int k, int I) {
@@ -1323,10 +1334,16 @@ static int resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t i
                              int32_t H, int32_t I, const void* shared_w13, const void* shared_w2,
                              const void* shared_gate, void* out, int32_t accumulate,
                              int32_t* err_word, void* workspace, size_t workspace_bytes,
-                             int32_t fetch_ctas, int32_t stages, const void* l2_warm,
-                             size_t l2_warm_bytes, d3_stream_t stream) {
+                             int32_t fetch_ctas, int32_t stages, const void* const* l2_warm,
+                             const size_t* l2_warm_bytes, int32_t n_windows,
+                             d3_stream_t stream) {
   D3_CHECK_ARG(L && ids && x && weights && out && err_word, "d3_resolve_fetch_moe: null pointer");
-  D3_CHECK_ARG(l2_warm || !l2_warm_bytes, "d3_resolve_fetch_moe_l2warm: null window");
+  D3_CHECK_ARG(n_windows >= 0 && n_windows <= kMaxWarmWindows,
+               "d3_resolve_fetch_moe_l2warm: n_windows must be in [0, %d]", kMaxWarmWindows);
+  D3_CHECK_ARG(n_windows == 0 || (l2_warm && l2_warm_bytes),
+               "d3_resolve_fetch_moe_l2warm: null window arrays");
+  for (int w = 0; w < n_windows; ++w)
+    D3_CHECK_ARG(l2_warm[w] || !l2_warm_bytes[w], "d3_resolve_fetch_moe_l2warm: null window");
   D3_CHECK_ARG(stages >= 1 && stages <= 7, "stages must be a non-empty mask of 1, 2, 4");
   D3_CHECK_ARG(k >= 1 && k <= 64, "k must be in [1, 64] (got %d)", k);
   if (!gemv_shapes_ok(k, H, I))
@@ -1390,8 +1407,17 @@ static int resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t i
   o.early_mask = (1u << 0) | (1u << 2);
   o.vecA = (b13 + bs13) / 16;
   o.err = err_word; o.err_code = 41; o.budget_ns = kOverlapWaitBudgetNs;
-  o.warm = static_cast<const char*>(l2_warm);
-  o.warm_lines = (unsigned long long)(l2_warm_bytes >> 7);
+  {
+    unsigned long long end = 0;
+    for (int w = 0; w < n_windows; ++w) {
+      const unsigned long long lines = (unsigned long long)(l2_warm_bytes[w] >> 7);
+      if (!lines) continue;
+      end += lines;
+      o.warm[o.n_warm] = static_cast<const char*>(l2_warm[w]);
+      o.warm_end[o.n_warm] = end;
+      ++o.n_warm;
+    }
+  }
   const int grid = 2 * num_sms();
   cudaError_t e;
   const bool pdl = pdl_enabled() && (stages & 1);
@@ -1413,7 +1439,7 @@ int d3_resolve_fetch_moe(const d3_layer_cache* L, const void* ids, int32_t ids_b
                          int32_t fetch_ctas, int32_t stages, d3_stream_t stream) {
   return resolve_fetch_moe(L, ids, ids_bytes, k, x, weights, weights_f32, H, I, shared_w13,
                            shared_w2, shared_gate, out, accumulate, err_word, workspace,
-                           workspace_bytes, fetch_ctas, stages, nullptr, 0, stream);
+                           workspace_bytes, fetch_ctas, stages, nullptr, nullptr, 0, stream);
 }
 
 int d3_resolve_fetch_moe_l2warm(const d3_layer_cache* L, const void* ids, int32_t ids_bytes,
@@ -1422,11 +1448,13 @@ int d3_resolve_fetch_moe_l2warm(const d3_layer_cache* L, const void* ids, int32_
                                 const void* shared_w13, const void* shared_w2,
                                 const void* shared_gate, void* out, int32_t accumulate,
                                 int32_t* err_word, void* workspace, size_t workspace_bytes,
-                                int32_t fetch_ctas, int32_t stages, const void* l2_warm,
-                                size_t l2_warm_bytes, d3_stream_t stream) {
+                                int32_t fetch_ctas, int32_t stages,
+                                const void* const* l2_warm, const size_t* l2_warm_bytes,
+                                int32_t n_windows, d3_stream_t stream) {
   return resolve_fetch_moe(L, ids, ids_bytes, k, x, weights, weights_f32, H, I, shared_w13,
                            shared_w2, shared_gate, out, accumulate, err_word, workspace,
-                           workspace_bytes, fetch_ctas, stages, l2_warm, l2_warm_bytes, stream);
+                           workspace_bytes, fetch_ctas, stages, l2_warm, l2_warm_bytes, n_windows,
+                           stream);
 }
 
 int d3_moe_fp8_forward_p2p(const void* x, const void* ids, int32_t ids_bytes,

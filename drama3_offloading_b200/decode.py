@@ -78,12 +78,14 @@ class DecodeStack:
                  policy: str = "lru", seed: int = 0, fill: str = "random", group=None,
                  local_rank: int = 0, trace_offset: int = 0, overlap: bool = True,
                  kv_context: int = KV_CONTEXT, host_per_node: bool = True,
-                 l2_warm_mib: float = 85.0):
+                 l2_warm_mib: float = 85.0, l2_warm_gate: bool = True):
         self.device = dev = torch.device(device)
         self.overlap = overlap
         # with the overlapped fetch: MiB of the next layer's first dense weight
         # hinted into L2 while this layer's fetch holds the host link
         self.l2_warm_bytes = int(l2_warm_mib * (1 << 20))
+        # ... and the next layer's router gate weight with it
+        self.l2_warm_gate = l2_warm_gate
         self.L, self.E, self.H, self.I, self.k = layers, experts, hidden, inter, topk
         per_expert = 2 * inter * hidden + hidden * inter + 4 * (2 * inter * hidden + hidden * inter) // (128 * 128)
         self.capacity = capacity or max(1, int(cache_gib * (1 << 30)) // (layers * per_expert))
@@ -157,10 +159,15 @@ class DecodeStack:
         if self.overlap:
             # allocator, then fetch + gate/up in one launch, then the down
             # projection (the timing sample brackets the fetch launch alone)
-            warm = self.up[(l + 1) % self.L] if self.l2_warm_bytes else None
+            nxt = (l + 1) % self.L
+            warm, caps = [], []
+            if self.l2_warm_gate:
+                warm.append(self.gate[nxt]); caps.append(None)
+            if self.l2_warm_bytes:
+                warm.append(self.up[nxt]); caps.append(self.l2_warm_bytes)
             run = lambda stages: devcache.dev_resolve_fetch_moe(
                 ex, cur_ids[l], h, self.wts, out=h, accumulate=True, shared=self.shared[l],
-                stages=stages, l2_warm=warm, l2_warm_bytes=self.l2_warm_bytes)
+                stages=stages, l2_warm=warm or None, l2_warm_bytes=caps or None)
             if events is None:
                 run(7)
                 return

@@ -197,17 +197,18 @@ def dev_resolve_and_fetch(experts, topk_ids: torch.Tensor, stream=None) -> torch
 def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
                           topk_weights: torch.Tensor, out: torch.Tensor | None = None,
                           accumulate: bool = False, shared: tuple | None = None,
-                          stream=None, stages: int = 7, l2_warm: torch.Tensor | None = None,
-                          l2_warm_bytes: int | None = None) -> torch.Tensor:
+                          stream=None, stages: int = 7, l2_warm=None,
+                          l2_warm_bytes=None) -> torch.Tensor:
     """One decode row through the cache: resolve ``topk_ids`` [1, k], fetch the
     misses while the gate/up products of the resident experts run, then the
     down projection into ``out`` (bf16 [1, H]; added to it with
     ``accumulate``).  ``shared=(w13_s, w2_s, gate_s)`` adds the shared expert
     inside the same launches.  Sync-free and graph-capturable.  ``stages``
     masks the launches issued (1 allocator, 2 fetch + gate/up, 4 down
-    projection; 7 = all), to time them apart.  ``l2_warm`` (a contiguous
-    device tensor of static weights the next launches read, e.g. the next
-    layer's dense weights): its first ``l2_warm_bytes`` (all by default) are
+    projection; 7 = all), to time them apart.  ``l2_warm``: a contiguous
+    device tensor, or a list of up to 4, of static weights the next launches
+    read (e.g. the next layer's router gate and dense weights); the first
+    ``l2_warm_bytes`` (an int, or one per tensor; None = all) of each are
     hinted into L2 while the fetch holds the host link."""
     from . import moe
     ids = _ids_arg(topk_ids)
@@ -242,11 +243,20 @@ def dev_resolve_fetch_moe(experts, topk_ids: torch.Tensor, x: torch.Tensor,
     if l2_warm is None:
         _lib.call("d3_resolve_fetch_moe", *args, _lib.stream_ptr(stream))
     else:
-        if not l2_warm.is_cuda or not l2_warm.is_contiguous():
-            raise ValueError("l2_warm must be a contiguous device tensor")
-        nb = l2_warm.numel() * l2_warm.element_size()
-        nb = nb if l2_warm_bytes is None else max(0, min(nb, int(l2_warm_bytes)))
-        _lib.call("d3_resolve_fetch_moe_l2warm", *args, _lib.ptr(l2_warm), nb,
+        ts = list(l2_warm) if isinstance(l2_warm, (list, tuple)) else [l2_warm]
+        caps = (list(l2_warm_bytes) if isinstance(l2_warm_bytes, (list, tuple))
+                else [l2_warm_bytes] * len(ts))
+        if not 1 <= len(ts) <= 4 or len(caps) != len(ts):
+            raise ValueError("l2_warm: 1 to 4 tensors, l2_warm_bytes one per tensor")
+        ptrs = (ctypes.c_void_p * len(ts))()
+        nbs = (ctypes.c_size_t * len(ts))()
+        for i, (t, cap) in enumerate(zip(ts, caps)):
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError("l2_warm tensors must be contiguous device tensors")
+            nb = t.numel() * t.element_size()
+            ptrs[i] = t.data_ptr()
+            nbs[i] = nb if cap is None else max(0, min(nb, int(cap)))
+        _lib.call("d3_resolve_fetch_moe_l2warm", *args, ptrs, nbs, len(ts),
                   _lib.stream_ptr(stream))
     return out
 

@@ -154,21 +154,22 @@ D3_API int d3_resolve_fetch_moe(const d3_layer_cache* layer, const void* ids, in
                                 int32_t* err_word, void* workspace, size_t workspace_bytes,
                                 int32_t fetch_ctas, int32_t stages, d3_stream_t stream);
 
-/* d3_resolve_fetch_moe plus an L2 warm window: while the fetch holds the host
- * link, the gate/up CTAs that have finished hint [l2_warm, l2_warm +
- * l2_warm_bytes) into L2 (whole 128-byte lines; a hint, never waited on).
- * Meant for static weights the next launches read (the next layer's dense
- * weights), which HBM, idle during the host-bound fetch, then serves from L2.
- * l2_warm may be NULL only with l2_warm_bytes = 0.  No counterpart in the
- * reference. */
+/* d3_resolve_fetch_moe plus L2 warm windows: while the fetch holds the host
+ * link, the gate/up CTAs that have finished hint the n_windows (<= 4) ranges
+ * [l2_warm[w], l2_warm[w] + l2_warm_bytes[w]) into L2 (whole 128-byte lines;
+ * a hint, never waited on).  Meant for static weights the next launches read
+ * (the next layer's router gate and first dense weight), which HBM, idle
+ * during the host-bound fetch, then serves from L2.  The two arrays are host
+ * memory, read during the call.  No counterpart in the reference. */
 D3_API int d3_resolve_fetch_moe_l2warm(const d3_layer_cache* layer, const void* ids,
                                        int32_t ids_bytes, int32_t k, const void* x,
                                        const void* weights, int32_t weights_f32, int32_t H,
                                        int32_t I, const void* shared_w13, const void* shared_w2,
                                        const void* shared_gate, void* out, int32_t accumulate,
                                        int32_t* err_word, void* workspace, size_t workspace_bytes,
-                                       int32_t fetch_ctas, int32_t stages, const void* l2_warm,
-                                       size_t l2_warm_bytes, d3_stream_t stream);
+                                       int32_t fetch_ctas, int32_t stages,
+                                       const void* const* l2_warm, const size_t* l2_warm_bytes,
+                                       int32_t n_windows, d3_stream_t stream);
 
 /* Only the fetch half of d3_resolve_fetch: copy the jobs already queued in
  * layer->fetch_slot / fetch_expert / *nmiss (e.g. by d3_resolve_slots or a

@@ -267,29 +267,34 @@ def test_fetch_gate_up_overlap_matches_separate_launches(cap, shared, acc, fetch
 
 
 def test_l2_warm_window_changes_nothing_but_timing():
-    """d3_resolve_fetch_moe_l2warm (the fused decode call with an L2 warm
-    window) gives the slots and bits of d3_resolve_fetch_moe, step after
-    step; the window's bytes are untouched."""
+    """d3_resolve_fetch_moe_l2warm (the fused decode call with L2 warm
+    windows: one, two, ragged sizes) gives the slots and bits of
+    d3_resolve_fetch_moe, step after step; the windows' bytes are untouched."""
     E, H, I = 64, 2048, 512
     ref = synth.make_experts(E, seed=13, device="cuda", style="test")
     a, b = ref.to("cpu").pin(), ref.to("cpu").pin()
     devcache.init_dev_cache(a, DEV, 12)
     devcache.init_dev_cache(b, DEV, 12)
     warm = torch.randn(3 << 20, device=DEV).to(torch.bfloat16)   # 6 MiB of "next-layer weights"
-    warm0 = warm.clone()
+    gate = torch.randn(256, 2048, device=DEV).to(torch.bfloat16)  # a second window (1 MiB)
+    warm0, gate0 = warm.clone(), gate.clone()
     g = torch.Generator().manual_seed(77)
     for step in range(20):
         x = torch.randn(1, H, generator=g).to(torch.bfloat16).to(DEV)
         ids = torch.randperm(E, generator=g)[:8].unsqueeze(0).to(DEV)
         w = torch.rand(1, 8, generator=g).to(DEV)
         nb = None if step % 2 else (step * 65537) % (6 << 20)   # whole window / ragged sizes
-        out_a = devcache.dev_resolve_fetch_moe(a, ids, x, w, l2_warm=warm, l2_warm_bytes=nb)
+        if step % 3 == 2:   # two windows
+            out_a = devcache.dev_resolve_fetch_moe(a, ids, x, w, l2_warm=[gate, warm],
+                                                   l2_warm_bytes=[None, nb])
+        else:
+            out_a = devcache.dev_resolve_fetch_moe(a, ids, x, w, l2_warm=warm, l2_warm_bytes=nb)
         out_b = devcache.dev_resolve_fetch_moe(b, ids, x, w)
         torch.cuda.synchronize()
         assert torch.equal(a._dc_out, b._dc_out), f"step {step}"
         assert torch.equal(out_a, out_b), f"step {step}"
     moe.check_errors(DEV)
-    assert torch.equal(warm, warm0)
+    assert torch.equal(warm, warm0) and torch.equal(gate, gate0)
 
 
 @pytest.mark.parametrize("T", [1, 5])   # CUDA-core path / tensor-core path
