@@ -102,6 +102,22 @@ def test_folded_entry_points_validate_without_gpu():
     assert call(d, 8, 2048, 512, ctypes.c_size_t(64)) == -7   # workspace too small
     d.nbuf = 3
     assert call(d, 8, 2048, 512, ws) == -1          # not the 4-buffer layout
+    d.nbuf = 4
+    # d3_resolve_fetch_moe_l2warm: the window list, then the same checks
+    ptrs = (P * 5)(16, 16, 16, 16, 16)
+    nbs = (ctypes.c_size_t * 5)(1 << 20, 4096, 128, 0, 7)
+    warm = lambda desc, k, pp, nn, n: lib.d3_resolve_fetch_moe_l2warm(
+        ctypes.byref(desc), z, 4, k, z, z, 1, 2048, 512, None, None, None, z, 0, z, z, ws, 0, 3,
+        pp, nn, n, P(0))
+    assert warm(d, 8, ptrs, nbs, 5) == -1           # more than 4 windows
+    assert warm(d, 8, None, None, 2) == -1          # null window arrays
+    assert warm(d, 8, ptrs, nbs, -1) == -1
+    nulls = (P * 2)(16, 0)
+    assert warm(d, 8, nulls, nbs, 2) == -1          # null window with bytes
+    d.capacity = 4
+    assert warm(d, 8, ptrs, nbs, 4) == -5           # then the plain call's checks: capacity < k
+    assert b"capacity" in lib.d3_last_error()
+    d.capacity = 12
     # d3_moe_fp8_forward_p2p: T must be n_ranks * cap, ranks in range
     arr = (P * 2)(16, 16)
     p2p = lambda T, n_ranks, rank, cap: lib.d3_moe_fp8_forward_p2p(
